@@ -1,0 +1,311 @@
+// extern "C" entry points of libbgattn.so: argument validation (mirroring the engine's
+// validation throws) and dispatch to the sm_100a kernels.  See include/bgattn.h.
+#include <math.h>
+
+#include "attn.h"
+#include "kv.h"
+
+using namespace bg;
+
+namespace {
+
+bool kv_mode_ok(uint32_t m) { return m <= BG_KV_Q8R; }
+
+bool d_ok(uint32_t D) { return D == 64 || D == 128 || D == 256; }
+
+// engine.ts:232-235 (head_dim limits, H % KV), :372-373 (q8 needs D % 32).
+int check_attn(const bg_attn_params *p, const bg_kv_cache *kv) {
+  if (!p || !kv) return BG_EINVAL;
+  if (p->H == 0 || p->KV == 0 || p->H % p->KV) return BG_EINVAL;
+  if (!d_ok(p->D)) return BG_EUNSUPPORTED;
+  if (!kv_mode_ok(kv->mode)) return BG_EINVAL;
+  if (kv->mode == BG_KV_Q8R && p->D % 128) return BG_EINVAL;
+  if ((kv->mode == BG_KV_Q8 || kv->mode == BG_KV_Q8R) && (!kv->Ks || !kv->Vs)) return BG_EINVAL;
+  if (!kv->K || !kv->V) return BG_EINVAL;
+  if (p->Ltot != p->posBase + p->S) return BG_EINVAL;
+  if (kv->window) {
+    if ((uint64_t)kv->sinks + kv->window > kv->seq_stride) return BG_EINVAL;
+    if (p->Ltot > kv->sinks + kv->window) return BG_EINVAL;
+  } else if (p->Ltot > kv->seq_stride) {
+    return BG_EINVAL;
+  }
+  return BG_OK;
+}
+
+KVView make_view(const bg_kv_cache *kv, uint32_t KV, uint32_t row_offset) {
+  KVView v;
+  v.K = kv->K;
+  v.V = kv->V;
+  v.Ks = kv->Ks;
+  v.Vs = kv->Vs;
+  v.seq_stride = kv->seq_stride;
+  v.sinks = kv->sinks;
+  v.window = kv->window;
+  v.ring_head = kv->window ? kv->ring_head % kv->window : 0;
+  v.KV = KV;
+  v.row_offset = row_offset;
+  return v;
+}
+
+size_t part_bytes(uint32_t nsplit, uint64_t rows, uint32_t D) { return (size_t)nsplit * rows * (D + 2) * sizeof(float); }
+
+int run_attention(const bg_attn_params *p, uint32_t batch, const void *q, uint32_t q_dtype, const bg_kv_cache *kv,
+                  const float *cosT, const float *sinT, float scale, uint32_t pos_lo, uint32_t pos_hi,
+                  uint32_t row_offset, float *partials_out, const float *gate, void *out, uint32_t out_dtype,
+                  void *ws, size_t ws_bytes, cudaStream_t st) {
+  AttnArgs a;
+  a.q = q;
+  a.q_f16 = q_dtype == BG_DT_F16;
+  a.kv = make_view(kv, p->KV, row_offset);
+  a.mode = (int)kv->mode;
+  a.cosT = cosT;
+  a.sinT = sinT;
+  a.scale = scale > 0.f ? scale : 1.0f / sqrtf((float)p->D);
+  a.B = batch;
+  a.S = p->S;
+  a.H = p->H;
+  a.KV = p->KV;
+  a.D = p->D;
+  a.posBase = p->posBase;
+  a.pos_lo = pos_lo;
+  a.pos_hi = pos_hi;
+  const uint64_t rows = (uint64_t)batch * p->S * p->H;
+  const uint32_t L = pos_hi > pos_lo ? pos_hi - pos_lo : 1;
+  a.nsplit = attn_num_splits(batch, p->S, p->H, p->KV, p->D, L);
+  a.chunk = (L + a.nsplit - 1) / a.nsplit;
+  if (ws_bytes < part_bytes(a.nsplit, rows, p->D) || (!ws && rows)) return BG_ENOMEM;
+  a.partials = static_cast<float *>(ws);
+  int rc = launch_attn_tc(a, st);
+  if (rc == BG_EUNSUPPORTED) rc = launch_attn_generic(a, st);
+  if (rc) return rc;
+  if (partials_out) return launch_lse_merge(a.partials, a.nsplit, (uint32_t)rows, p->D, nullptr, partials_out, -1, st);
+  return launch_lse_merge(a.partials, a.nsplit, (uint32_t)rows, p->D, gate, out, out_dtype == BG_DT_F16, st);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *bg_strerror(int code) {
+  switch (code) {
+    case BG_OK: return "ok";
+    case BG_EINVAL: return "invalid argument";
+    case BG_ENOMEM: return "workspace too small";
+    case BG_ELAUNCH: return "CUDA launch failed";
+    case BG_ETIMEOUT: return "device wait timed out";
+    case BG_EUNSUPPORTED: return "unsupported shape or mode";
+    default: return "unknown error";
+  }
+}
+
+int bg_version(void) { return 1; }
+
+size_t bg_attention_workspace_size(const bg_attn_params *p, uint32_t batch) {
+  if (!p || !p->KV || !p->H) return 0;
+  const uint32_t L = p->Ltot ? p->Ltot : 1;
+  const uint32_t ns = attn_num_splits(batch, p->S, p->H, p->KV, p->D, L);
+  return part_bytes(ns, (uint64_t)batch * p->S * p->H, p->D);
+}
+
+int bg_attention(const bg_attn_params *p, uint32_t batch, const void *q, uint32_t q_dtype, const bg_kv_cache *kv,
+                 const float *cosT, const float *sinT, float scale, const float *gate, void *out, uint32_t out_dtype,
+                 void *workspace, size_t workspace_bytes, bg_stream_t stream) {
+  int rc = check_attn(p, kv);
+  if (rc) return rc;
+  if (!q || !out || q_dtype > BG_DT_F16 || out_dtype > BG_DT_F16) return BG_EINVAL;
+  if ((cosT == nullptr) != (sinT == nullptr)) return BG_EINVAL;
+  if (batch == 0 || p->S == 0) return BG_OK;
+  return run_attention(p, batch, q, q_dtype, kv, cosT, sinT, scale, 0, p->Ltot, 0, nullptr, gate, out, out_dtype,
+                       workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+int bg_attention_partials(const bg_attn_params *p, uint32_t batch, const void *q, uint32_t q_dtype,
+                          const bg_kv_cache *kv, const float *cosT, const float *sinT, float scale, uint32_t pos_lo,
+                          uint32_t pos_hi, float *partials, void *workspace, size_t workspace_bytes,
+                          bg_stream_t stream) {
+  if (!p || !kv || !q || !partials) return BG_EINVAL;
+  if (p->H == 0 || p->KV == 0 || p->H % p->KV || !kv_mode_ok(kv->mode)) return BG_EINVAL;
+  if (!d_ok(p->D)) return BG_EUNSUPPORTED;
+  if (p->Ltot != p->posBase + p->S || pos_lo > pos_hi || pos_hi > p->Ltot) return BG_EINVAL;
+  if (kv->window) return BG_EUNSUPPORTED;
+  if (pos_hi - pos_lo > kv->seq_stride) return BG_EINVAL;
+  if ((cosT == nullptr) != (sinT == nullptr)) return BG_EINVAL;
+  if (batch == 0 || p->S == 0) return BG_OK;
+  if (pos_hi == pos_lo) {  // nothing attended here: an empty partial (l = 0)
+    const uint64_t n = (uint64_t)batch * p->S * p->H * (p->D + 2);
+    return cudaMemsetAsync(partials, 0, n * sizeof(float), (cudaStream_t)stream) == cudaSuccess ? BG_OK : BG_ELAUNCH;
+  }
+  return run_attention(p, batch, q, q_dtype, kv, cosT, sinT, scale, pos_lo, pos_hi, pos_lo, partials, nullptr,
+                       nullptr, 0, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+int bg_lse_merge(const float *partials, uint32_t nsplit, uint32_t rows, uint32_t D, const float *gate, void *out,
+                 uint32_t out_dtype, bg_stream_t stream) {
+  if (!partials || !out || nsplit == 0 || D == 0 || out_dtype > BG_DT_F16) return BG_EINVAL;
+  return launch_lse_merge(partials, nsplit, rows, D, gate, out, out_dtype == BG_DT_F16, (cudaStream_t)stream);
+}
+
+int bg_kv_append(const bg_kv_cache *kv, uint32_t which, uint32_t batch, const void *src, uint32_t src_dtype,
+                 uint32_t S, uint32_t KV, uint32_t D, uint32_t pos0, bg_stream_t stream) {
+  if (!kv || !src || which > 1 || src_dtype > BG_DT_F16 || !kv_mode_ok(kv->mode) || KV == 0) return BG_EINVAL;
+  if (!d_ok(D)) return BG_EUNSUPPORTED;
+  if (kv->mode == BG_KV_Q8R && D % 128) return BG_EINVAL;
+  if ((which ? kv->V : kv->K) == nullptr) return BG_EINVAL;
+  if ((kv->mode == BG_KV_Q8 || kv->mode == BG_KV_Q8R) && (which ? kv->Vs : kv->Ks) == nullptr) return BG_EINVAL;
+  const uint64_t cap = kv->window ? (uint64_t)kv->sinks + kv->window : kv->seq_stride;
+  if ((uint64_t)pos0 + S > cap) return BG_EINVAL;  // the engine's ensureKvCapacity / evictFor precondition
+  if (batch == 0 || S == 0) return BG_OK;
+  return launch_kv_append(make_view(kv, KV, 0), (int)kv->mode, D, src, src_dtype == BG_DT_F16, batch, S, pos0,
+                          (int)which, (cudaStream_t)stream);
+}
+
+int bg_rmsnorm_rope(const float *x, uint32_t batch, uint32_t R, uint32_t D, const float *gamma, const float *cos,
+                    const float *sin, float eps, float *y, const bg_kv_cache *kv, uint32_t pos, bg_stream_t stream) {
+  if (!x || !gamma || (!y && !kv) || ((cos == nullptr) != (sin == nullptr))) return BG_EINVAL;
+  if (!d_ok(D)) return BG_EUNSUPPORTED;
+  KVView v = {};
+  int mode = 0;
+  if (kv) {
+    if (!kv_mode_ok(kv->mode) || !kv->K) return BG_EINVAL;
+    if ((kv->mode == BG_KV_Q8 || kv->mode == BG_KV_Q8R) && !kv->Ks) return BG_EINVAL;
+    if (kv->mode == BG_KV_Q8R && D % 128) return BG_EINVAL;
+    const uint64_t cap = kv->window ? (uint64_t)kv->sinks + kv->window : kv->seq_stride;
+    if (pos >= cap) return BG_EINVAL;
+    v = make_view(kv, R, 0);
+    mode = (int)kv->mode;
+  }
+  if (batch == 0 || R == 0) return BG_OK;
+  return launch_rmsnorm_rope(x, batch, R, D, gamma, cos, sin, eps, y, v, mode, pos, kv != nullptr,
+                             (cudaStream_t)stream);
+}
+
+int bg_kv_evict(const bg_kv_cache *kv, uint32_t batch, uint32_t KV, uint32_t D, uint32_t fill, uint32_t need,
+                uint32_t max_seq_len, uint32_t *new_fill, bg_stream_t stream) {
+  if (!kv || !new_fill || !kv_mode_ok(kv->mode) || kv->window || KV == 0) return BG_EINVAL;
+  if (fill < kv->sinks || fill > kv->seq_stride || max_seq_len < kv->sinks) return BG_EINVAL;
+  const uint32_t S0 = kv->sinks;
+  const uint32_t recent = fill - S0;
+  const uint32_t quarter = (max_seq_len - S0 + 3) / 4;  // ceil((maxSeqLen - SINKS) / 4)
+  uint32_t batchn = need > quarter ? need : quarter;
+  if (batchn > recent) batchn = recent;
+  const int64_t keep = (int64_t)recent - batchn;
+  if (keep <= 0) {
+    *new_fill = S0;
+    return BG_OK;
+  }
+  const uint64_t esz = kv->mode == BG_KV_F32 ? 4 : kv->mode == BG_KV_F16 ? 2 : 1;
+  const uint64_t row_bytes = (uint64_t)KV * D * esz;
+  const uint64_t srow_bytes =
+      kv->mode == BG_KV_Q8 ? (uint64_t)KV * (D / 32) * 4 : kv->mode == BG_KV_Q8R ? (uint64_t)KV * (D / 128) * 4 : 0;
+  struct Arr {
+    void *p;
+    uint64_t rb;
+  } arrs[4] = {{kv->K, row_bytes}, {kv->V, row_bytes}, {kv->Ks, srow_bytes}, {kv->Vs, srow_bytes}};
+  // Move [S0+batch, fill) down to S0 in ascending chunks of `batch` rows: within a chunk the
+  // source and destination ranges are disjoint, and a chunk's source is only overwritten by a
+  // later chunk (stream order), which is what the reference's scratch bounce guarantees.
+  for (int ai = 0; ai < 4; ++ai) {
+    if (!arrs[ai].p || !arrs[ai].rb) continue;
+    const uint64_t rb = arrs[ai].rb;
+    for (uint64_t c = 0; c < (uint64_t)keep; c += batchn) {
+      const uint64_t n = ((uint64_t)keep - c) < batchn ? ((uint64_t)keep - c) : batchn;
+      int rc = launch_copy_rows(arrs[ai].p, kv->seq_stride * rb, batch, (S0 + c) * rb, (S0 + batchn + c) * rb, n * rb,
+                                (cudaStream_t)stream);
+      if (rc) return rc;
+    }
+  }
+  *new_fill = S0 + (uint32_t)keep;
+  return BG_OK;
+}
+
+int bg_kv_ring_evict(bg_kv_cache *kv, uint32_t fill, uint32_t need, uint32_t max_seq_len, uint32_t *new_fill) {
+  if (!kv || !new_fill || kv->window == 0 || fill < kv->sinks || max_seq_len < kv->sinks) return BG_EINVAL;
+  const uint32_t S0 = kv->sinks;
+  const uint32_t recent = fill - S0;
+  const uint32_t quarter = (max_seq_len - S0 + 3) / 4;
+  uint32_t batchn = need > quarter ? need : quarter;
+  if (batchn > recent) batchn = recent;
+  const int64_t keep = (int64_t)recent - batchn;
+  if (keep <= 0) {
+    *new_fill = S0;
+    kv->ring_head = 0;
+    return BG_OK;
+  }
+  kv->ring_head = (uint32_t)(((uint64_t)kv->ring_head + batchn) % kv->window);
+  *new_fill = S0 + (uint32_t)keep;
+  return BG_OK;
+}
+
+int bg_deltanet_gbeta(const float *a, const float *b, const float *a_neg, const float *dt_bias, uint32_t S, uint32_t H,
+                      float *out, bg_stream_t stream) {
+  if (!a || !b || !a_neg || !dt_bias || !out) return BG_EINVAL;
+  return launch_gbeta(a, b, a_neg, dt_bias, S, H, out, (cudaStream_t)stream);
+}
+
+int bg_deltanet_recur(const uint32_t params[8], const float *q, const float *k, const float *v, const float *g,
+                      const float *beta, const float *state_in, float *core, float *state_out, bg_stream_t stream) {
+  if (!params || !q || !k || !v || !g || !beta || !core || !state_out) return BG_EINVAL;
+  DeltaArgs a = {};
+  a.S = params[0];
+  a.H = params[1];
+  a.DK = params[2];
+  a.DV = params[3];
+  a.HK = params[4];
+  a.betaOff = params[5];
+  a.loadState = params[6];
+  a.tOff = params[7];
+  if (!a.H || !a.HK || a.H % a.HK || !a.DV || a.DV > 256) return BG_EINVAL;
+  if (a.loadState && !state_in) return BG_EINVAL;
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.g = g;
+  a.beta = beta;
+  a.state_in = state_in;
+  a.state_out = state_out;
+  a.core = core;
+  return launch_deltanet(a, (cudaStream_t)stream);
+}
+
+int bg_deltanet_norm_gate(const float *core, const float *z, const float *gamma, uint32_t rows, uint32_t DV, float eps,
+                          float *y, bg_stream_t stream) {
+  if (!core || !z || !gamma || !y || !DV) return BG_EINVAL;
+  return launch_norm_gate(core, z, gamma, rows, DV, eps, y, (cudaStream_t)stream);
+}
+
+int bg_deltanet_fused(uint32_t S, uint32_t H, uint32_t HK, uint32_t DK, uint32_t DV, const float *q, const float *k,
+                      const float *v, const float *a, const float *b, const float *a_neg, const float *dt_bias,
+                      const float *z, const float *gamma, float eps, const float *state_in, float *state_out,
+                      float *core, float *y, bg_stream_t stream) {
+  if (!q || !k || !v || !a || !b || !a_neg || !dt_bias || !z || !gamma || !y || !state_out) return BG_EINVAL;
+  if (!H || !HK || H % HK || !DV || DV > 256) return BG_EINVAL;
+  DeltaArgs d = {};
+  d.S = S;
+  d.H = H;
+  d.HK = HK;
+  d.DK = DK;
+  d.DV = DV;
+  d.loadState = state_in != nullptr;
+  d.q = q;
+  d.k = k;
+  d.v = v;
+  d.a = a;
+  d.b = b;
+  d.a_neg = a_neg;
+  d.dt_bias = dt_bias;
+  d.z = z;
+  d.gamma = gamma;
+  d.eps = eps;
+  d.state_in = state_in;
+  d.state_out = state_out;
+  d.core = core;
+  d.y = y;
+  return launch_deltanet(d, (cudaStream_t)stream);
+}
+
+int bg_gate_sigmoid(const float *x, const float *gate, uint32_t n, float *y, bg_stream_t stream) {
+  if (!x || !gate || !y) return BG_EINVAL;
+  return launch_gate_sigmoid(x, gate, n, y, (cudaStream_t)stream);
+}
+
+}  // extern "C"

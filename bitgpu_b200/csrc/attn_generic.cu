@@ -1,0 +1,287 @@
+// CUDA-core split-KV GQA attention over f32 / f16 / q8 / q8r caches, with optional rope-at-read
+// (rolling-window mode) and ring-mapped slots.  It is the production path for the f32 cache
+// and for rope-at-read, and the reference path every other kernel is cross-checked against.
+//
+// Math per query row (shaders/attention_sg.wgsl:31-44): online softmax over the row's cache
+// positions, scores (q.k)*scale, f32 throughout.  Scores are carried in log2 units (scale is
+// pre-multiplied by log2 e) so the exponentials are exp2f.
+//
+// Work decomposition: one CTA per (KV split, sequence x kv head, chunk of RB query rows).  All
+// rows of a chunk share the CTA's K/V reads (a row is (query token, head of the GQA group)), so a
+// cache row is read once per group instead of once per head as in the reference.  4 warps walk
+// interleaved positions; a lane owns D/32 contiguous dims (vector loads); per-warp states are
+// merged through shared memory and written as split partials for bg::launch_lse_merge.
+#include <math.h>
+
+#include "attn.h"
+
+namespace bg {
+namespace {
+
+template <int MODE, int DPL>
+__device__ __forceinline__ void load_row(const KVView &kv, bool is_v, uint64_t row, int lane,
+                                         float (&x)[DPL]) {
+  constexpr int D = DPL * 32;
+  const uint64_t off = row * D + (uint64_t)lane * DPL;
+  if constexpr (MODE == BG_KV_F32) {
+    load_f32<DPL>(static_cast<const float *>(is_v ? kv.V : kv.K) + off, x);
+  } else if constexpr (MODE == BG_KV_F16) {
+    load_f16<DPL>(static_cast<const __half *>(is_v ? kv.V : kv.K) + off, x);
+  } else {
+    int8_t c[DPL];
+    load_i8<DPL>(static_cast<const int8_t *>(is_v ? kv.V : kv.K) + off, c);
+    const float *sc = is_v ? kv.Vs : kv.Ks;
+    if constexpr (MODE == BG_KV_Q8) {
+      const float s = sc[row * (D / 32) + (lane * DPL) / 32];
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) x[i] = snorm8(c[i]) * s;
+    } else {  // q8r: one absmax/127 scale per 128 elements
+      const float s = sc[row * (D / 128) + (lane * DPL) / 128];
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) x[i] = (float)c[i] * s;
+    }
+  }
+}
+
+template <int MODE, int D, bool ROLL, int RB>
+__global__ void __launch_bounds__(128) attn_generic_kernel(AttnArgs a) {
+  constexpr int DPL = D / 32;
+  constexpr int NW = 4;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t split = blockIdx.x;
+  const uint32_t b = blockIdx.y / a.KV, kvh = blockIdx.y % a.KV;
+  const uint32_t G = a.H / a.KV;
+  const uint32_t rows = a.S * G;
+  const uint32_t r0 = blockIdx.z * RB;
+
+  // rows of this CTA: r -> (qi = r / G, head = kvh*G + r % G)
+  float q[RB][DPL];
+  uint32_t lastpos[RB];
+  uint32_t maxlast = 0;
+  const float sl2 = a.scale * kLog2e;
+#pragma unroll
+  for (int r = 0; r < RB; ++r) {
+    const uint32_t rr = r0 + r;
+    if (rr < rows) {
+      const uint32_t qi = rr / G, h = kvh * G + rr % G;
+      const uint64_t qoff = (((uint64_t)b * a.S + qi) * a.H + h) * D + lane * DPL;
+      if (a.q_f16) load_f16<DPL>(static_cast<const __half *>(a.q) + qoff, q[r]);
+      else load_f32<DPL>(static_cast<const float *>(a.q) + qoff, q[r]);
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) q[r][i] *= sl2;
+      lastpos[r] = a.posBase + qi;
+      maxlast = max(maxlast, lastpos[r]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) q[r][i] = 0.f;
+      lastpos[r] = 0;
+    }
+  }
+  const bool row_valid_any = r0 < rows;
+  uint32_t lo = a.pos_lo + split * a.chunk;
+  uint32_t hi = min(a.pos_hi, lo + a.chunk);
+  hi = min(hi, maxlast + 1);
+
+  float m[RB], l[RB], acc[RB][DPL];
+#pragma unroll
+  for (int r = 0; r < RB; ++r) {
+    m[r] = kNegBig;
+    l[r] = 0.f;
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) acc[r][i] = 0.f;
+  }
+
+  if (row_valid_any) {
+    for (uint32_t j = lo + warp; j < hi; j += NW) {
+      const uint64_t row = cache_row(a.kv, b, j, kvh);
+      float k[DPL], v[DPL];
+      load_row<MODE, DPL>(a.kv, false, row, lane, k);
+      load_row<MODE, DPL>(a.kv, true, row, lane, v);
+      if constexpr (ROLL) {
+        // rope-at-read by logical slot j (attention_sg_roll.wgsl:42-50): partner dim d +- D/2
+        // is held by lane ^ 16; rotate_half gives -k[d+half] below half, +k[d-half] above.
+        constexpr int HALF = D / 2;
+        const float *cs = a.cosT + (uint64_t)j * HALF + (lane & 15) * DPL;
+        const float *sn = a.sinT + (uint64_t)j * HALF + (lane & 15) * DPL;
+        float c[DPL], s[DPL];
+        load_f32<DPL>(cs, c);
+        load_f32<DPL>(sn, s);
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) {
+          const float p = __shfl_xor_sync(0xffffffffu, k[i], 16);
+          const float rot = lane < 16 ? -p : p;
+          k[i] = k[i] * c[i] + rot * s[i];
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < RB; ++r) {
+        float part = 0.f;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) part = fmaf(q[r][i], k[i], part);
+        float sc = warp_sum(part);
+        if (j > lastpos[r]) sc = -INFINITY;
+        const float mn = fmaxf(m[r], sc);
+        const float corr = exp2f(m[r] - mn);
+        const float p = exp2f(sc - mn);
+        l[r] = l[r] * corr + p;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) acc[r][i] = fmaf(acc[r][i], corr, p * v[i]);
+        m[r] = mn;
+      }
+    }
+  }
+
+  // merge the 4 warps' states: shared [NW][RB][D + 2]
+  extern __shared__ float sh[];
+  float *mine = sh + (size_t)warp * RB * (D + 2);
+#pragma unroll
+  for (int r = 0; r < RB; ++r) {
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) mine[r * (D + 2) + lane * DPL + i] = acc[r][i];
+    if (lane == 0) {
+      mine[r * (D + 2) + D] = m[r];
+      mine[r * (D + 2) + D + 1] = l[r];
+    }
+  }
+  __syncthreads();
+  const uint32_t nrows_total = a.B * a.S * a.H;
+  for (int idx = threadIdx.x; idx < RB * D; idx += blockDim.x) {
+    const int r = idx / D, d = idx % D;
+    const uint32_t rr = r0 + r;
+    if (rr >= rows) continue;
+    float M = kNegBig;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, sh[(w * RB + r) * (D + 2) + D]);
+    float o = 0.f, L = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      const float *st = sh + (w * RB + r) * (D + 2);
+      const float f = exp2f(st[D] - M);
+      o = fmaf(st[d], f, o);
+      L = fmaf(st[D + 1], f, L);
+    }
+    const uint32_t qi = rr / G, h = kvh * G + rr % G;
+    const uint64_t grow = ((uint64_t)b * a.S + qi) * a.H + h;
+    float *dst = a.partials + ((uint64_t)split * nrows_total + grow) * (D + 2);
+    dst[d] = o;
+    if (d == 0) {
+      dst[D] = L > 0.f ? M * kLn2 : -INFINITY;
+      dst[D + 1] = L;
+    }
+  }
+}
+
+// Combine split partials [nsplit][rows][D+2] -> out[rows][D], optional sigmoid gate.
+__global__ void lse_merge_kernel(const float *__restrict__ part, uint32_t nsplit, uint32_t rows,
+                                 uint32_t D, const float *__restrict__ gate, void *out, int out_f16) {
+  const uint32_t row = blockIdx.x;
+  extern __shared__ float w[];  // [nsplit] weights, then total
+  __shared__ float Ltot, Mx;
+  if (threadIdx.x == 0) {
+    float M = -INFINITY;
+    for (uint32_t s = 0; s < nsplit; ++s) {
+      const float *p = part + ((uint64_t)s * rows + row) * (D + 2);
+      if (p[D + 1] > 0.f) M = fmaxf(M, p[D]);
+    }
+    float L = 0.f;
+    for (uint32_t s = 0; s < nsplit; ++s) {
+      const float *p = part + ((uint64_t)s * rows + row) * (D + 2);
+      const float f = p[D + 1] > 0.f ? expf(p[D] - M) : 0.f;
+      w[s] = f;
+      L = fmaf(p[D + 1], f, L);
+    }
+    Ltot = L;
+    Mx = M;
+  }
+  __syncthreads();
+  for (uint32_t d = threadIdx.x; d < D; d += blockDim.x) {
+    float o = 0.f;
+    for (uint32_t s = 0; s < nsplit; ++s) {
+      const float f = w[s];
+      if (f != 0.f) o = fmaf(part[((uint64_t)s * rows + row) * (D + 2) + d], f, o);
+    }
+    if (out_f16 < 0) {  // merge into one partial row (o, m, l): used by split-KV slices
+      float *dst = static_cast<float *>(out) + (uint64_t)row * (D + 2);
+      dst[d] = o;
+      if (d == 0) {
+        dst[D] = Ltot > 0.f ? Mx : -INFINITY;
+        dst[D + 1] = Ltot;
+      }
+      continue;
+    }
+    o = o / Ltot;
+    if (gate) o = o / (1.0f + expf(-gate[(uint64_t)row * D + d]));
+    if (out_f16) static_cast<__half *>(out)[(uint64_t)row * D + d] = __float2half_rn(o);
+    else static_cast<float *>(out)[(uint64_t)row * D + d] = o;
+  }
+}
+
+template <int MODE, int D, bool ROLL>
+int launch_rb(const AttnArgs &a, cudaStream_t st) {
+  const uint32_t rows = a.S * (a.H / a.KV);
+  constexpr int RBMAX = D >= 256 ? 4 : 8;
+  auto go = [&](auto rbc) -> int {
+    constexpr int RB = decltype(rbc)::value;
+    dim3 grid(a.nsplit, a.B * a.KV, (rows + RB - 1) / RB);
+    const size_t smem = (size_t)4 * RB * (D + 2) * sizeof(float);
+    auto kern = attn_generic_kernel<MODE, D, ROLL, RB>;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    kern<<<grid, 128, smem, st>>>(a);
+    return cudaGetLastError() == cudaSuccess ? BG_OK : BG_ELAUNCH;
+  };
+  if (rows <= 1) return go(std::integral_constant<int, 1>{});
+  if (rows <= 2) return go(std::integral_constant<int, 2>{});
+  if (rows <= 4 || RBMAX == 4) return go(std::integral_constant<int, (RBMAX < 4 ? RBMAX : 4)>{});
+  return go(std::integral_constant<int, RBMAX>{});
+}
+
+template <int MODE, int D>
+int launch_roll(const AttnArgs &a, cudaStream_t st) {
+  return a.cosT ? launch_rb<MODE, D, true>(a, st) : launch_rb<MODE, D, false>(a, st);
+}
+
+template <int MODE>
+int launch_d(const AttnArgs &a, cudaStream_t st) {
+  switch (a.D) {
+    case 64: return launch_roll<MODE, 64>(a, st);
+    case 128: return launch_roll<MODE, 128>(a, st);
+    case 256: return launch_roll<MODE, 256>(a, st);
+    default: return BG_EUNSUPPORTED;
+  }
+}
+
+}  // namespace
+
+uint32_t attn_num_splits(uint32_t B, uint32_t S, uint32_t H, uint32_t KV, uint32_t D, uint32_t L) {
+  // Enough CTAs to cover 148 SMs a few times over, but never a split shorter than 64
+  // positions (each split costs a partial row write + merge read).
+  const uint32_t G = H / KV;
+  const uint32_t rb = D >= 256 ? 4 : 8;
+  const uint64_t base = (uint64_t)B * KV * ((S * G + rb - 1) / rb);
+  const uint64_t want = (4 * 148 + base - 1) / base;
+  const uint64_t maxs = (L + 63) / 64;
+  uint64_t n = want < maxs ? want : maxs;
+  if (n < 1) n = 1;
+  if (n > 256) n = 256;
+  return (uint32_t)n;
+}
+
+int launch_attn_generic(const AttnArgs &a, cudaStream_t st) {
+  switch (a.mode) {
+    case BG_KV_F32: return launch_d<BG_KV_F32>(a, st);
+    case BG_KV_F16: return launch_d<BG_KV_F16>(a, st);
+    case BG_KV_Q8: return launch_d<BG_KV_Q8>(a, st);
+    case BG_KV_Q8R: return a.D % 128 ? BG_EUNSUPPORTED : launch_d<BG_KV_Q8R>(a, st);
+    default: return BG_EINVAL;
+  }
+}
+
+int launch_lse_merge(const float *partials, uint32_t nsplit, uint32_t rows, uint32_t D,
+                     const float *gate, void *out, int out_f16, cudaStream_t st) {
+  if (rows == 0) return BG_OK;
+  const int threads = D >= 128 ? 128 : 64;
+  lse_merge_kernel<<<rows, threads, nsplit * sizeof(float), st>>>(partials, nsplit, rows, D, gate, out, out_f16);
+  return cudaGetLastError() == cudaSuccess ? BG_OK : BG_ELAUNCH;
+}
+
+}  // namespace bg

@@ -1,0 +1,224 @@
+// Gated DeltaNet kernels: the recurrent scan (deltanet_recur.wgsl) with optional fused g/beta
+// prologue (deltanet_gbeta.wgsl) and gated-RMSNorm epilogue (deltanet_norm_gate.wgsl), plus the
+// stand-alone elementwise kernels and the attention output gate (gate_sigmoid.wgsl).
+//
+// Recurrence layout: the per-head state S[dk][dv] splits by value column -- every column evolves
+// independently (kv = Kn.S[:,dv], delta[dv], S[:,dv] += Kn*delta[dv]) -- so a CTA owns 32
+// columns of one head and a head spreads over DV/32 CTAs (4 for DV=128: 192 CTAs for the 27B's
+// 48 value heads instead of 48).  Within a CTA, warp w holds rows [w*DK/4, (w+1)*DK/4) of the 32
+// columns in registers (lane = column), so the state streams HBM -> registers -> HBM once per
+// launch.  The two reductions over dk per token (kv and the output) cross the 4 warps through
+// shared memory.  With the fused norm-gate the DV/32 CTAs of a head form a thread-block cluster
+// and add their per-token sums of squares through distributed shared memory.
+#include <cooperative_groups.h>
+#include <math.h>
+
+#include "kv.h"
+
+namespace cg = cooperative_groups;
+
+namespace bg {
+namespace {
+
+__device__ __forceinline__ float softplus_stable(float x) { return fmaxf(x, 0.f) + logf(1.0f + expf(-fabsf(x))); }
+__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+template <int DK, bool FUSED>
+__global__ void __launch_bounds__(128) deltanet_kernel(DeltaArgs a) {
+  constexpr int RPW = DK / 4;      // state rows per warp
+  constexpr int KPL = DK / 32;     // k/q values per lane for the norms
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t cg_idx = blockIdx.x;          // column group
+  const uint32_t h = blockIdx.y;
+  const uint32_t hk = h % a.HK;                // "tile" GQA (deltanet_recur.wgsl:27)
+  const uint32_t c = cg_idx * 32 + lane;       // value column
+  const bool cval = c < a.DV;
+
+  __shared__ float kn_s[4][DK], qn_s[4][DK];   // per-warp copies (no block barrier needed)
+  __shared__ float red_kv[4][32], red_o[4][32];
+  __shared__ float ss_part[2];                 // fused: this CTA's sum of squares, double-buffered
+
+  float s[RPW];
+  const uint64_t sbase = (uint64_t)h * DK * a.DV;
+#pragma unroll
+  for (int i = 0; i < RPW; ++i) {
+    const uint32_t dk = warp * RPW + i;
+    s[i] = (a.loadState && a.state_in && cval) ? a.state_in[sbase + (uint64_t)dk * a.DV + c] : 0.f;
+  }
+  const float qscale = 1.0f / sqrtf((float)DK);
+
+  for (uint32_t t = 0; t < a.S; ++t) {
+    const uint32_t tt = t + a.tOff;
+    const uint64_t base = (uint64_t)tt * a.H + h;
+    const uint64_t basek = (uint64_t)tt * a.HK + hk;
+    // l2norm(k), l2norm(q)/sqrt(dk): each warp computes both norms on its own (no barrier)
+    float kv_[KPL], qv_[KPL];
+#pragma unroll
+    for (int i = 0; i < KPL; ++i) {
+      kv_[i] = a.k[basek * DK + lane * KPL + i];
+      qv_[i] = a.q[basek * DK + lane * KPL + i];
+    }
+    float sk = 0.f, sq = 0.f;
+#pragma unroll
+    for (int i = 0; i < KPL; ++i) {
+      sk = fmaf(kv_[i], kv_[i], sk);
+      sq = fmaf(qv_[i], qv_[i], sq);
+    }
+    sk = warp_sum(sk);
+    sq = warp_sum(sq);
+    const float ik = 1.0f / sqrtf(sk + 1e-6f);
+    const float iq = (1.0f / sqrtf(sq + 1e-6f)) * qscale;
+#pragma unroll
+    for (int i = 0; i < KPL; ++i) {
+      kn_s[warp][lane * KPL + i] = kv_[i] * ik;
+      qn_s[warp][lane * KPL + i] = qv_[i] * iq;
+    }
+    float gt, bt;
+    if constexpr (FUSED) {
+      const float x = a.a[base] + a.dt_bias[h];
+      gt = expf(a.a_neg[h] * softplus_stable(x));
+      bt = sigmoidf_(a.b[base]);
+    } else {
+      gt = expf(a.g[base]);
+      bt = a.beta[a.betaOff + base];
+    }
+    __syncwarp();
+    float part = 0.f;
+#pragma unroll
+    for (int i = 0; i < RPW; ++i) {
+      s[i] *= gt;
+      part = fmaf(s[i], kn_s[warp][warp * RPW + i], part);
+    }
+    red_kv[warp][lane] = part;
+    __syncthreads();
+    const float kvv = red_kv[0][lane] + red_kv[1][lane] + red_kv[2][lane] + red_kv[3][lane];
+    const float vv = cval ? a.v[base * a.DV + c] : 0.f;
+    const float delta = (vv - kvv) * bt;
+    float po = 0.f;
+#pragma unroll
+    for (int i = 0; i < RPW; ++i) {
+      s[i] = fmaf(kn_s[warp][warp * RPW + i], delta, s[i]);
+      po = fmaf(s[i], qn_s[warp][warp * RPW + i], po);
+    }
+    red_o[warp][lane] = po;
+    __syncthreads();
+    const float o = red_o[0][lane] + red_o[1][lane] + red_o[2][lane] + red_o[3][lane];
+    if (warp == 0 && cval && a.core) a.core[base * a.DV + c] = o;
+    if constexpr (FUSED) {
+      cg::cluster_group cl = cg::this_cluster();
+      if (warp == 0) {
+        const float sq2 = warp_sum(cval ? o * o : 0.f);
+        if (lane == 0) ss_part[t & 1] = sq2;
+      }
+      cl.sync();
+      if (warp == 0) {
+        float tot = 0.f;
+        const unsigned nr = cl.num_blocks();
+        for (unsigned r = 0; r < nr; ++r) tot += cl.map_shared_rank(&ss_part[t & 1], r)[0];
+        const float inv = 1.0f / sqrtf(tot / (float)a.DV + a.eps);
+        if (cval) {
+          const float zz = a.z[base * a.DV + c];
+          a.y[base * a.DV + c] = a.gamma[c] * (o * inv) * (zz / (1.0f + expf(-zz)));
+        }
+      }
+    }
+  }
+  if constexpr (FUSED) cg::this_cluster().sync();  // no CTA exits while a peer may read its smem
+  if (cval && a.state_out) {
+#pragma unroll
+    for (int i = 0; i < RPW; ++i) {
+      const uint32_t dk = warp * RPW + i;
+      a.state_out[sbase + (uint64_t)dk * a.DV + c] = s[i];
+    }
+  }
+}
+
+__global__ void gbeta_kernel(const float *a, const float *b, const float *an, const float *dt, uint32_t S, uint32_t H,
+                             float *out) {
+  const uint32_t n = S * H;
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint32_t h = i % H;
+  out[i] = an[h] * softplus_stable(a[i] + dt[h]);
+  out[n + i] = sigmoidf_(b[i]);
+}
+
+// one warp per row (deltanet_norm_gate.wgsl:19-31)
+__global__ void norm_gate_kernel(const float *core, const float *z, const float *gamma, uint32_t rows, uint32_t DV,
+                                 float eps, float *y) {
+  const uint32_t row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float *cr = core + (uint64_t)row * DV;
+  float ss = 0.f;
+  for (uint32_t i = lane; i < DV; i += 32) ss = fmaf(cr[i], cr[i], ss);
+  ss = warp_sum(ss);
+  const float inv = 1.0f / sqrtf(ss / (float)DV + eps);
+  for (uint32_t i = lane; i < DV; i += 32) {
+    const float zz = z[(uint64_t)row * DV + i];
+    y[(uint64_t)row * DV + i] = gamma[i] * (cr[i] * inv) * (zz / (1.0f + expf(-zz)));
+  }
+}
+
+__global__ void gate_sigmoid_kernel(const float *x, const float *g, uint32_t n, float *y) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = x[i] / (1.0f + expf(-g[i]));
+}
+
+template <int DK>
+int launch_dk(const DeltaArgs &a, cudaStream_t st) {
+  const uint32_t ncg = (a.DV + 31) / 32;
+  const bool fused = a.z != nullptr;
+  if (!fused) {
+    deltanet_kernel<DK, false><<<dim3(ncg, a.H), 128, 0, st>>>(a);
+    return cudaGetLastError() == cudaSuccess ? BG_OK : BG_ELAUNCH;
+  }
+  if (ncg > 8) return BG_EUNSUPPORTED;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ncg, a.H);
+  cfg.blockDim = dim3(128);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = ncg;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, deltanet_kernel<DK, true>, a);
+  return e == cudaSuccess ? BG_OK : BG_ELAUNCH;
+}
+
+}  // namespace
+
+int launch_deltanet(const DeltaArgs &a, cudaStream_t st) {
+  if (a.S == 0) return BG_OK;
+  switch (a.DK) {
+    case 64: return launch_dk<64>(a, st);
+    case 128: return launch_dk<128>(a, st);
+    default: return BG_EUNSUPPORTED;
+  }
+}
+
+int launch_gbeta(const float *a, const float *b, const float *an, const float *dt, uint32_t S, uint32_t H, float *out,
+                 cudaStream_t st) {
+  const uint32_t n = S * H;
+  if (!n) return BG_OK;
+  gbeta_kernel<<<(n + 255) / 256, 256, 0, st>>>(a, b, an, dt, S, H, out);
+  return cudaGetLastError() == cudaSuccess ? BG_OK : BG_ELAUNCH;
+}
+
+int launch_norm_gate(const float *core, const float *z, const float *gamma, uint32_t rows, uint32_t DV, float eps,
+                     float *y, cudaStream_t st) {
+  if (!rows) return BG_OK;
+  norm_gate_kernel<<<(rows * 32 + 255) / 256, 256, 0, st>>>(core, z, gamma, rows, DV, eps, y);
+  return cudaGetLastError() == cudaSuccess ? BG_OK : BG_ELAUNCH;
+}
+
+int launch_gate_sigmoid(const float *x, const float *g, uint32_t n, float *y, cudaStream_t st) {
+  if (!n) return BG_OK;
+  gate_sigmoid_kernel<<<(n + 255) / 256, 256, 0, st>>>(x, g, n, y);
+  return cudaGetLastError() == cudaSuccess ? BG_OK : BG_ELAUNCH;
+}
+
+}  // namespace bg

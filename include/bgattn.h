@@ -1,0 +1,150 @@
+/* bgattn.h -- C ABI of the B200 (sm_100a) attention hot path for bitgpu.
+ *
+ * Every entry point replaces one WebGPU dispatch (or one engine helper) of bitgpu's attention
+ * path; the reference interface is cited beside each declaration as file:line of the bitgpu
+ * source tree.  Conventions shared by all entry points:
+ *   - all pointers are DEVICE pointers owned by the caller; no entry point allocates device
+ *     memory (scratch comes in through `workspace`);
+ *   - work is enqueued asynchronously on `stream` (a cudaStream_t, NULL = legacy stream);
+ *   - return 0 on success or a negative BG_E* code (never aborts); bg_strerror() names it;
+ *   - float math is IEEE f32 (no fast-math); KV storage codecs follow the reference exactly.
+ *
+ * KV cache layout (reference: shaders/attention_sg.wgsl:11-12, src/engine.ts:1072-1079):
+ *   element (seq b, position p, kv head h, dim d) lives at
+ *     row = (b*seq_stride + phys(p))*KV + h,  offset = row*D + d
+ *   f32/f16: one element per value; q8: int8 codes (== packed u32 snorm8 words, component 0 in
+ *   the low byte, shaders/copy_kv8.wgsl:39) plus one f32 scale per 32-element block at
+ *   Ks[row*(D/32) + d/32] (shaders/copy_kv8.wgsl:35); q8r (extra mode, not in the reference):
+ *   one absmax/127 scale per row of 128 at Ks[row*(D/128) + d/128].
+ *   phys(p) = p when window == 0; otherwise (rolling window with `sinks` pinned slots,
+ *   overflow 'sinks', src/engine.ts:1180-1214) phys(p) = p < sinks ? p
+ *   : sinks + (ring_head + p - sinks) % window, so eviction can advance ring_head instead of
+ *   moving bytes (bg_kv_ring_evict) while logical slots keep the reference's order.
+ */
+#ifndef BGATTN_H
+#define BGATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void *bg_stream_t; /* cudaStream_t */
+
+enum {
+  BG_OK = 0,
+  BG_EINVAL = -1,       /* bad parameters (the engine's validation throws, engine.ts:232-235,372) */
+  BG_ENOMEM = -2,       /* workspace too small */
+  BG_ELAUNCH = -3,      /* CUDA launch / runtime error */
+  BG_ETIMEOUT = -4,     /* a bounded device wait gave up */
+  BG_EUNSUPPORTED = -5  /* shape / mode combination not built */
+};
+
+enum { BG_KV_F32 = 0, BG_KV_F16 = 1, BG_KV_Q8 = 2, BG_KV_Q8R = 3 };
+enum { BG_DT_F32 = 0, BG_DT_F16 = 1 };
+
+/* == struct Params of shaders/attention_sg.wgsl:7 (also _wg, _kv16, _kv8, _roll variants). */
+typedef struct {
+  uint32_t S, H, KV, D, posBase, Ltot;
+} bg_attn_params;
+
+/* One layer's K/V cache for `batch` sequences (src/engine.ts:1051-1079 Kc/Vc/Ksc/Vsc). */
+typedef struct {
+  void *K, *V;         /* f32 / f16 values or int8 codes */
+  float *Ks, *Vs;      /* q8 / q8r scales, NULL otherwise */
+  uint64_t seq_stride; /* positions per sequence slab (the cache capacity) */
+  uint32_t mode;       /* BG_KV_* */
+  uint32_t sinks, window, ring_head; /* rolling window; window == 0: linear */
+} bg_kv_cache;
+
+const char *bg_strerror(int code);
+int bg_version(void);
+
+/* ---- attention (decode S small, prefill / PLD verify S > 1) -------------------------------
+ * Replaces the ATT dispatch of src/engine.ts:1543 (fused decode) and :1580 (prefill), i.e.
+ * shaders/attention_{sg,wg}{,_kv16,_kv8}.wgsl, and the head_dim-256 hybrid kernels
+ * attention_online_cache{,_kv8}.wgsl via engine.ts:1487-1489, with gate_sigmoid.wgsl
+ * (engine.ts:1491) fused when `gate` is non-NULL.
+ * q [batch][S][H][D] (q_dtype), out [batch][S][H][D] (out_dtype); query row qi of every
+ * sequence attends logical cache positions 0..posBase+qi (Ltot must be posBase+S).
+ * scale == 0 selects 1/sqrt(D) (attention_sg.wgsl:24); the online kernels pass it explicitly.
+ * cosT/sinT non-NULL selects rope-at-read of unroped keys by logical slot, tables
+ * [positions][D/2] (the attention_*_roll.wgsl kernels, bindings engine.ts:1395-1399).
+ * gate [batch][S][H][D] f32 or NULL: out = att / (1 + exp(-gate)). */
+size_t bg_attention_workspace_size(const bg_attn_params *p, uint32_t batch);
+int bg_attention(const bg_attn_params *p, uint32_t batch, const void *q, uint32_t q_dtype,
+                 const bg_kv_cache *kv, const float *cosT, const float *sinT, float scale,
+                 const float *gate, void *out, uint32_t out_dtype, void *workspace,
+                 size_t workspace_bytes, bg_stream_t stream);
+
+/* ---- split-KV across GPUs (no reference counterpart: the reference is single-device) ----
+ * Partial attention over the cache positions [pos_lo, pos_hi) that THIS caller holds: the
+ * local cache `kv` stores position pos_lo at physical row 0.  partials
+ * [batch*S*H][D+2] = (unnormalised o[D], running max m, sum l), m = -inf / l = 0 for rows
+ * that attend nothing in the slice.  bg_lse_merge combines nsplit such blocks laid out
+ * [nsplit][rows][D+2] (e.g. an all-gather result) into out, applying the optional gate. */
+int bg_attention_partials(const bg_attn_params *p, uint32_t batch, const void *q,
+                          uint32_t q_dtype, const bg_kv_cache *kv, const float *cosT,
+                          const float *sinT, float scale, uint32_t pos_lo, uint32_t pos_hi,
+                          float *partials, void *workspace, size_t workspace_bytes,
+                          bg_stream_t stream);
+int bg_lse_merge(const float *partials, uint32_t nsplit, uint32_t rows, uint32_t D,
+                 const float *gate, void *out, uint32_t out_dtype, bg_stream_t stream);
+
+/* ---- KV cache writers ---------------------------------------------------------------------
+ * bg_kv_append: appendKV(pass, src, which, li, rows, dstRow0) of src/engine.ts:1385-1393
+ * (copy.wgsl / copy_kv16.wgsl / copy_kv8.wgsl).  which: 0 = K, 1 = V.  src [batch][S][KV][D]
+ * (src_dtype) is written at logical positions pos0..pos0+S-1 (dstRow0 = pos0*KV). */
+int bg_kv_append(const bg_kv_cache *kv, uint32_t which, uint32_t batch, const void *src,
+                 uint32_t src_dtype, uint32_t S, uint32_t KV, uint32_t D, uint32_t pos0,
+                 bg_stream_t stream);
+
+/* bg_rmsnorm_rope: rmsnorm_rope_sg{,_kv16,_kv8}.wgsl (engine.ts:1529-1540): per head row
+ * y = rmsnorm(x)*gamma rotated by (cos, sin) ([D] tables of this position; NULL/NULL = no
+ * rotation, the sink-mode cos=1/sin=0 binding of engine.ts:1533).  x [batch][R][D]; the result
+ * goes to y [batch][R][D] when y != NULL and/or into the cache at logical position `pos`
+ * (R == KV rows) when kv != NULL. */
+int bg_rmsnorm_rope(const float *x, uint32_t batch, uint32_t R, uint32_t D, const float *gamma,
+                    const float *cos, const float *sin, float eps, float *y,
+                    const bg_kv_cache *kv, uint32_t pos, bg_stream_t stream);
+
+/* bg_kv_evict: evict() of src/engine.ts:1188-1212 (batched sink compaction, bytes moved, no
+ * re-rope / requantise) for a linear cache; *new_fill receives the engine's return value. */
+int bg_kv_evict(const bg_kv_cache *kv, uint32_t batch, uint32_t KV, uint32_t D, uint32_t fill,
+                uint32_t need, uint32_t max_seq_len, uint32_t *new_fill, bg_stream_t stream);
+/* bg_kv_ring_evict: the same schedule on a ring cache (window > 0): advances kv->ring_head,
+ * moves no bytes.  Host-only bookkeeping. */
+int bg_kv_ring_evict(bg_kv_cache *kv, uint32_t fill, uint32_t need, uint32_t max_seq_len,
+                     uint32_t *new_fill);
+
+/* ---- gated DeltaNet ----------------------------------------------------------------------
+ * bg_deltanet_gbeta: deltanet_gbeta.wgsl (engine.ts:1438); out [2*S*H] = [g ; beta]. */
+int bg_deltanet_gbeta(const float *a, const float *b, const float *a_neg, const float *dt_bias,
+                      uint32_t S, uint32_t H, float *out, bg_stream_t stream);
+/* bg_deltanet_recur: deltanet_recur.wgsl (engine.ts:1446-1458); params == its Params
+ * {S, H, DK, DV, HK, betaOff, loadState, tOff}.  q,k [*, HK, DK]; v [*, H, DV]; g and beta
+ * [*, H] (beta read at beta[betaOff + ...], so it may point into the gbeta buffer);
+ * state [H][DK][DV]; core [*, H, DV].  state_out may alias state_in. */
+int bg_deltanet_recur(const uint32_t params[8], const float *q, const float *k, const float *v,
+                      const float *g, const float *beta, const float *state_in, float *core,
+                      float *state_out, bg_stream_t stream);
+/* bg_deltanet_norm_gate: deltanet_norm_gate.wgsl (engine.ts:1462). */
+int bg_deltanet_norm_gate(const float *core, const float *z, const float *gamma, uint32_t rows,
+                          uint32_t DV, float eps, float *y, bg_stream_t stream);
+/* bg_deltanet_fused: gbeta -> recurrence -> gated norm in one launch (engine.ts:1438-1462 for
+ * one segment).  state_in NULL = zero state; y [S][H][DV] normed output; core may be NULL. */
+int bg_deltanet_fused(uint32_t S, uint32_t H, uint32_t HK, uint32_t DK, uint32_t DV,
+                      const float *q, const float *k, const float *v, const float *a,
+                      const float *b, const float *a_neg, const float *dt_bias, const float *z,
+                      const float *gamma, float eps, const float *state_in, float *state_out,
+                      float *core, float *y, bg_stream_t stream);
+
+/* bg_gate_sigmoid: gate_sigmoid.wgsl (engine.ts:1491), y = x / (1 + exp(-gate)). */
+int bg_gate_sigmoid(const float *x, const float *gate, uint32_t n, float *y, bg_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* BGATTN_H */

@@ -1,0 +1,167 @@
+"""GPU parity: attention kernels (through the C ABI) vs the CPU oracle."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN
+from gpu_util import TOL, fill_cache, gate_ok, rand
+from oracle import attention as OA
+from oracle import rope as OR
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from bitgpu_b200 import ops
+    return ops
+
+
+def run_case(ops, mode, B, S, H, KV, D, pos_base, seed, q_dtype=torch.float32, gate=False, scale=0.0,
+             out_dtype=torch.float32, roll=False, window=0, ring_head=0, sinks=0, cap_extra=5):
+    rng = np.random.default_rng(seed)
+    L = pos_base + S
+    cache = ops.KVCache(B, L + cap_extra, KV, D, mode=mode, sinks=sinks, window=window, device="cuda")
+    cache.ring_head = ring_head
+    Kraw, Vraw = rand(rng, B, L, KV, D), rand(rng, B, L, KV, D)
+    Kd, Vd = fill_cache(cache, Kraw, Vraw)
+    q = rand(rng, B, S, H, D)
+    if q_dtype == torch.float16:
+        q = q.astype(np.float16).astype(np.float32)
+    g = rand(rng, B, S, H, D) if gate else None
+    cos_t = sin_t = None
+    if roll:
+        c, s = OR.synth_rope(D, L + 8, 1e6, "yarn", 4.0, 8192)
+        cos_t, sin_t = torch.from_numpy(c).cuda(), torch.from_numpy(s).cuda()
+    out = ops.attention(torch.from_numpy(q).to("cuda", q_dtype), cache, pos_base, scale=scale,
+                        gate=None if g is None else torch.from_numpy(g).cuda(), cos_t=cos_t, sin_t=sin_t,
+                        out_dtype=out_dtype)
+    out = out.float().cpu().numpy()
+    for b in range(B):
+        Kb = OA.rotate_keys_at_read(Kd[b], c, s) if roll else Kd[b]
+        exp = OA.attend(q[b], Kb, Vd[b], pos_base, scale=scale if scale else None,
+                        gate=None if g is None else g[b])
+        ok, mad, cos = gate_ok(out[b], exp, tol=TOL)
+        assert ok, (mode, b, mad, cos)
+    return out
+
+
+@pytest.mark.parametrize("mode", ["f32", "f16", "q8", "q8r"])
+@pytest.mark.parametrize("D", [64, 128, 256])
+def test_decode_modes(ops, mode, D):
+    if mode == "q8r" and D % 128:
+        pytest.skip("q8r needs D % 128 == 0")
+    run_case(ops, mode, B=2, S=1, H=8, KV=2, D=D, pos_base=777, seed=D)
+
+
+@pytest.mark.parametrize("mode", ["f32", "f16", "q8"])
+@pytest.mark.parametrize("S,H,KV,pos_base", [(3, 16, 8, 100), (9, 32, 8, 1500), (17, 24, 4, 0), (5, 6, 6, 63)])
+def test_multi_row_causal(ops, mode, S, H, KV, pos_base):
+    """PLD verify / prefill rows: row qi attends 0..posBase+qi (attention_sg.wgsl:21,31)."""
+    run_case(ops, mode, B=1, S=S, H=H, KV=KV, D=128, pos_base=pos_base, seed=S * 7 + H)
+
+
+def test_cfg1_shape(ops):
+    """Config 1: Qwen3-1.7B shape, 2048-position f32 cache, one query token."""
+    run_case(ops, "f32", B=1, S=1, H=16, KV=8, D=128, pos_base=2047, seed=1)
+
+
+def test_long_context_f16_q8(ops):
+    for mode in ("f16", "q8"):
+        run_case(ops, mode, B=2, S=1, H=32, KV=8, D=128, pos_base=32767, seed=2)
+
+
+def test_gated_d256(ops):
+    """27B gated attention shape (H24/KV4/D256) with the sigmoid gate fused in the merge."""
+    for mode in ("f32", "f16", "q8"):
+        run_case(ops, mode, B=1, S=2, H=24, KV=4, D=256, pos_base=4000, seed=3, gate=True,
+                 scale=float(1 / np.sqrt(256)))
+
+
+def test_f16_q_and_f16_out(ops):
+    run_case(ops, "f16", B=2, S=4, H=32, KV=8, D=128, pos_base=300, seed=4, q_dtype=torch.float16,
+             out_dtype=torch.float16)
+
+
+@pytest.mark.parametrize("mode", ["f32", "f16", "q8"])
+def test_roll_rope_at_read(ops, mode):
+    run_case(ops, mode, B=2, S=1, H=16, KV=8, D=128, pos_base=500, seed=5, roll=True)
+
+
+@pytest.mark.parametrize("mode", ["f16", "q8"])
+def test_roll_ring_wrapped(ops, mode):
+    """Ring layout with the head mid-window: logical slot order must not depend on it."""
+    run_case(ops, mode, B=2, S=1, H=16, KV=8, D=128, pos_base=299, seed=6, roll=True, sinks=4, window=296,
+             ring_head=123, cap_extra=0)
+
+
+def test_golden_gated_d256(ops):
+    z = np.load(os.path.join(GOLDEN, "ga_d256_gated.npz"))
+    S, H, D = z["q"].shape
+    KV = z["k"].shape[1]
+    cache = ops.KVCache(1, S, KV, D, mode="f32")
+    cache.K[0] = torch.from_numpy(z["k"]).cuda()
+    cache.V[0] = torch.from_numpy(z["v"]).cuda()
+    out = ops.attention(torch.from_numpy(z["q"])[None].cuda(), cache, 0, scale=float(1 / np.sqrt(D)),
+                        gate=torch.from_numpy(z["gate"])[None].cuda().contiguous())
+    ok, mad, cos = gate_ok(out[0].cpu().numpy(), z["expected"])
+    assert ok, (mad, cos)
+
+
+def test_golden_kernel_case_attention(ops):
+    """tools/gen-kernel-cases.py 'attention' case (head_dim 256) through the cache path."""
+    z = np.load(os.path.join(GOLDEN, "kc_attention.npz"))
+    S, H, KV, D = [int(x) for x in z["params"][:4]]
+    cache = ops.KVCache(1, S, KV, D, mode="f32")
+    cache.K[0] = torch.from_numpy(z["in1"].reshape(S, KV, D)).cuda()
+    cache.V[0] = torch.from_numpy(z["in2"].reshape(S, KV, D)).cuda()
+    out = ops.attention(torch.from_numpy(z["in0"].reshape(1, S, H, D)).cuda(), cache, 0, scale=float(z["params"][4]))
+    ok, mad, cos = gate_ok(out.cpu().numpy(), z["expected"])
+    assert ok, (mad, cos)
+
+
+def test_golden_plain_d128(ops):
+    z = np.load(os.path.join(GOLDEN, "ga_d128_plain.npz"))
+    S, H, D = z["q"].shape
+    KV = z["k"].shape[1]
+    for mode in ("f32", "f16"):
+        cache = ops.KVCache(1, S + 3, KV, D, mode=mode)
+        fill_cache(cache, z["k"][None], z["v"][None])
+        out = ops.attention(torch.from_numpy(z["q"])[None].cuda(), cache, 0)
+        ok, mad, cos = gate_ok(out[0].cpu().numpy(), z["expected"], tol=2e-3 if mode == "f16" else 1e-5)
+        assert ok, (mode, mad, cos)
+
+
+def test_split_partials_merge(ops):
+    """bg_attention_partials over disjoint slices + bg_lse_merge == full attention."""
+    rng = np.random.default_rng(9)
+    B, S, H, KV, D, pb = 1, 2, 24, 4, 256, 3000
+    L = pb + S
+    Kraw, Vraw = rand(rng, B, L, KV, D), rand(rng, B, L, KV, D)
+    q = torch.from_numpy(rand(rng, B, S, H, D)).cuda()
+    gate = torch.from_numpy(rand(rng, B, S, H, D)).cuda()
+    full = ops.KVCache(B, L, KV, D, mode="f16")
+    fill_cache(full, Kraw, Vraw)
+    ref = ops.attention(q, full, pb, gate=gate).cpu().numpy()
+    bounds = [0, 700, 1800, 1801, L]
+    parts = []
+    for lo, hi in zip(bounds[:-1], bounds[1:]):
+        c = ops.KVCache(B, max(hi - lo, 1), KV, D, mode="f16")
+        fill_cache(c, Kraw[:, lo:hi], Vraw[:, lo:hi])
+        parts.append(ops.attention_partials(q, c, pb, lo, hi))
+    out = ops.lse_merge(torch.stack(parts), (B, S, H, D), gate=gate).cpu().numpy()
+    assert np.abs(out - ref).max() < 1e-4
+
+
+def test_abi_errors(ops):
+    """Validation mirrors the engine's throws: H % KV, q8 head_dim, Ltot, capacity."""
+    from bitgpu_b200._lib import BgError
+    cache = ops.KVCache(1, 16, 3, 128, mode="f16")
+    q = torch.zeros(1, 1, 8, 128, device="cuda")
+    with pytest.raises(BgError):
+        ops.attention(q, cache, 0)          # 8 % 3 != 0
+    cache = ops.KVCache(1, 16, 2, 128, mode="f16")
+    with pytest.raises(BgError):
+        ops.attention(q, cache, 16)         # posBase + S > capacity

@@ -1,0 +1,127 @@
+"""GPU parity: gated DeltaNet kernels vs the oracle and the reference's golden vectors."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN
+from gpu_util import gate_ok, rand
+from oracle import deltanet as OD
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from bitgpu_b200 import ops
+    return ops
+
+
+def cu(x):
+    return torch.from_numpy(np.ascontiguousarray(x, np.float32)).cuda()
+
+
+def test_golden_kc_deltanet_recur(ops):
+    z = np.load(os.path.join(GOLDEN, "kc_deltanet_recur.npz"))
+    S, H, DK, DV, HK = [int(x) for x in z["params"][:5]]
+    core = torch.empty(S * H * DV, device="cuda")
+    st = torch.empty(H * DK * DV, device="cuda")
+    ops.deltanet_recur([S, H, DK, DV, HK, 0, 0, 0], cu(z["in0"]), cu(z["in1"]), cu(z["in2"]), cu(z["in3"]),
+                       cu(z["in4"]), cu(z["in5"]), core, st)
+    ok, mad, cos = gate_ok(core.cpu().numpy(), z["expected"])
+    assert ok, (mad, cos)
+
+
+def test_golden_gbeta_and_norm_gate(ops):
+    z = np.load(os.path.join(GOLDEN, "kc_gbeta.npz"))
+    S, H = [int(x) for x in z["params"][:2]]
+    out = ops.deltanet_gbeta(cu(z["in0"].reshape(S, H)), cu(z["in1"].reshape(S, H)), cu(z["in2"]), cu(z["in3"]))
+    assert gate_ok(out.cpu().numpy(), z["expected"], tol=1e-5)[0]
+    z = np.load(os.path.join(GOLDEN, "kc_norm_gate.npz"))
+    rows, DV = int(z["params"][0]), int(z["params"][1])
+    y = ops.deltanet_norm_gate(cu(z["in0"].reshape(rows, DV)), cu(z["in1"].reshape(rows, DV)), cu(z["in2"]),
+                               float(z["params"][2]))
+    assert gate_ok(y.cpu().numpy(), z["expected"], tol=1e-4)[0]
+
+
+def engine_schedule(S, flush=16):
+    """Sub-chunk sizes of engine.ts:1446-1452: odd chunk count, 8+8 split when needed."""
+    sizes = []
+    if -(-S // flush) % 2 == 0:
+        sizes += [flush // 2, flush // 2]
+    r = S - sum(sizes)
+    while r > 0:
+        sizes.append(min(r, flush))
+        r -= flush
+    return sizes
+
+
+def test_golden_s70_engine_subchunks(ops):
+    """The reference's recurrence over 70 tokens, run with the engine's ping-pong sub-chunk
+    cadence (RECUR_FLUSH=16, engine.ts:1446-1458) through bg_deltanet_recur."""
+    z = np.load(os.path.join(GOLDEN, "dn_delta_s70.npz"))
+    S, HK, DK = z["q"].shape
+    H, DV = z["v"].shape[1:]
+    g, beta = z["g"], z["beta"]
+    gb = cu(np.concatenate([g.ravel(), beta.ravel()]))
+    q, k, v = cu(z["q"]), cu(z["k"]), cu(z["v"])
+    core = torch.empty(S * H * DV, device="cuda")
+    halves = [torch.zeros(H * DK * DV, device="cuda"), torch.zeros(H * DK * DV, device="cuda")]
+    off = 0
+    sizes = engine_schedule(S)
+    assert len(sizes) % 2 == 1
+    for ci, n in enumerate(sizes):
+        cin, cout = halves[ci & 1], halves[(ci & 1) ^ 1]
+        ops.deltanet_recur([n, H, DK, DV, HK, S * H, 0 if ci == 0 else 1, off], q, k, v, gb, gb, cin, core, cout)
+        off += n
+    ok, mad, cos = gate_ok(core.cpu().numpy(), z["recurrent"])
+    assert ok, (mad, cos)
+    _, st = OD.recurrent(z["q"], z["k"], z["v"], g, beta)
+    assert np.abs(halves[1].cpu().numpy().reshape(st.shape) - st).max() < 1e-3
+
+
+def test_fused_equals_separate_27b_shape(ops):
+    """gbeta -> recur -> norm_gate fused (cluster DSMEM norm) == the oracle, 27B head counts."""
+    rng = np.random.default_rng(21)
+    S, HK, H, DK, DV, eps = 24, 16, 48, 128, 128, 1e-6
+    q, k = rand(rng, S, HK, DK), rand(rng, S, HK, DK)
+    v, z = rand(rng, S, H, DV), rand(rng, S, H, DV)
+    a, b = rand(rng, S, H), rand(rng, S, H)
+    a_neg = np.full(H, -1.0, np.float32)
+    dt = np.zeros(H, np.float32)
+    gamma = (1 + 0.1 * rng.standard_normal(DV)).astype(np.float32)
+    st0 = rand(rng, H, DK, DV, scale=0.05)
+    y, st, core = ops.deltanet_fused(cu(q), cu(k), cu(v), cu(a), cu(b), cu(a_neg), cu(dt), cu(z), cu(gamma), eps,
+                                     state_in=cu(st0), want_core=True)
+    g, beta = OD.gbeta(a, b, a_neg, dt)
+    ec, est = OD.recurrent(q, k, v, g, beta, state_in=st0)
+    ey = OD.norm_gate(ec.reshape(-1, DV), z.reshape(-1, DV), gamma, eps).reshape(S, H, DV)
+    assert gate_ok(core.cpu().numpy(), ec)[0]
+    ok, mad, cos = gate_ok(y.cpu().numpy(), ey)
+    assert ok, (mad, cos)
+    assert np.abs(st.cpu().numpy() - est).max() < 1e-3
+
+
+def test_decode_continuation(ops):
+    """Decode S=1 steps continuing a prefill state == one long recurrence."""
+    rng = np.random.default_rng(22)
+    S, HK, H, DK, DV = 12, 2, 6, 128, 128
+    q, k, v = rand(rng, S, HK, DK), rand(rng, S, HK, DK), rand(rng, S, H, DV)
+    g = (-np.logaddexp(0, rng.standard_normal((S, H)))).astype(np.float32)
+    beta = (1 / (1 + np.exp(-rng.standard_normal((S, H))))).astype(np.float32)
+    ec, est = OD.recurrent(q, k, v, g, beta)
+    st = torch.zeros(H * DK * DV, device="cuda")
+    core = torch.empty(S * H * DV, device="cuda")
+    gq, bq = cu(g), cu(beta)
+    for t in range(S):   # in-place state (state_out aliases state_in)
+        ops.deltanet_recur([1, H, DK, DV, HK, 0, 1, t], cu(q), cu(k), cu(v), gq, bq, st, core, st)
+    assert gate_ok(core.cpu().numpy(), ec)[0]
+    assert np.abs(st.cpu().numpy().reshape(est.shape) - est).max() < 1e-3
+
+
+def test_gate_sigmoid(ops):
+    rng = np.random.default_rng(23)
+    x, g = rand(rng, 1000), rand(rng, 1000, scale=4)
+    y = ops.gate_sigmoid(cu(x), cu(g)).cpu().numpy()
+    assert np.abs(y - x / (1 + np.exp(-g))).max() < 1e-6
