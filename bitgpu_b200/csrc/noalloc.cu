@@ -1,0 +1,59 @@
+// bg_attention_noalloc: the decode / prefill attention of bg_attention for callers that cannot
+// allocate device memory.
+//
+// bg_attention needs a caller-provided scratch buffer for its split-KV partial results.  Some
+// hosts cannot produce one: an engine whose device memory is entirely owned by another allocator
+// (a WebGPU-style host that hands the library only the buffers it already created, with no
+// allocator exposed across the binding), or a caller on a latency-critical token loop that must
+// not call cudaMalloc, which can synchronise the device.  For them this entry point keeps its
+// scratch in a fixed array compiled into the library (kNoAllocScratchBytes per GPU, resident on
+// every GPU that loads the library until the process exits) and allocates nothing at all.
+#include <mutex>
+
+#include "attn.h"
+
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = 8u << 20;  // 8 MiB per device
+
+// The scratch itself.  In host code this name is only a host-side stand-in for the symbol:
+// kernels must be given the device address from cudaGetSymbolAddress, never &g_noalloc_scratch.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_mu;
+void *g_scratch_ptr[kMaxDevices] = {};
+
+// Device address of the scratch on the current device, looked up once per device (with that
+// device current) and cached.  Returns nullptr on failure.
+void *scratch_for_current_device() {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_scratch_ptr[dev]) {
+    void *p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return nullptr;
+    g_scratch_ptr[dev] = p;
+  }
+  return g_scratch_ptr[dev];
+}
+
+}  // namespace
+
+extern "C" {
+
+int bg_attention_noalloc(const bg_attn_params *p, uint32_t batch, const void *q, uint32_t q_dtype,
+                         const bg_kv_cache *kv, const float *cosT, const float *sinT, float scale, const float *gate,
+                         void *out, uint32_t out_dtype, bg_stream_t stream) {
+  if (!p) return BG_EINVAL;
+  // Shapes whose partials do not fit the fixed scratch are rejected up front (BG_ENOMEM).
+  if (bg_attention_workspace_size(p, batch) > kNoAllocScratchBytes) return BG_ENOMEM;
+  void *ws = scratch_for_current_device();
+  if (!ws) return BG_ELAUNCH;
+  // Every partial row the merge reads is written earlier in the same call, so the scratch needs
+  // no clearing between calls.
+  return bg_attention(p, batch, q, q_dtype, kv, cosT, sinT, scale, gate, out, out_dtype, ws, kNoAllocScratchBytes,
+                      stream);
+}
+
+}  // extern "C"

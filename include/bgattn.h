@@ -79,6 +79,21 @@ int bg_attention(const bg_attn_params *p, uint32_t batch, const void *q, uint32_
                  const float *gate, void *out, uint32_t out_dtype, void *workspace,
                  size_t workspace_bytes, bg_stream_t stream);
 
+/* bg_attention_noalloc: bg_attention for callers that cannot allocate device memory.
+ * No counterpart in the reference (its kernels take every buffer from the engine).  Some hosts
+ * cannot hand over a scratch buffer: the engine's device memory may all belong to another
+ * allocator with none exposed across the binding, or the token loop may not call cudaMalloc
+ * (which can synchronise the device).  This variant takes no workspace: it uses a fixed 8 MiB
+ * scratch array compiled into the library, held on every GPU that loads the library until the
+ * process exits.  Same arguments and results as bg_attention minus the workspace; returns
+ * BG_ENOMEM when bg_attention_workspace_size(p, batch) exceeds 8 MiB.  The first call on a device
+ * looks up the array's device address with that device current (make that first call before
+ * any stream capture).  All calls share the one array: calls that overlap on the GPU (different
+ * streams, or several host threads) race on it and must be serialised by the caller. */
+int bg_attention_noalloc(const bg_attn_params *p, uint32_t batch, const void *q, uint32_t q_dtype,
+                         const bg_kv_cache *kv, const float *cosT, const float *sinT, float scale,
+                         const float *gate, void *out, uint32_t out_dtype, bg_stream_t stream);
+
 /* ---- split-KV across GPUs (no reference counterpart: the reference is single-device) ----
  * Partial attention over the cache positions [pos_lo, pos_hi) that THIS caller holds: the
  * local cache `kv` stores position pos_lo at physical row 0.  partials
