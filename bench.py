@@ -20,9 +20,7 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -42,11 +40,14 @@ def alg_bytes(mode, batch=B, ctx=L):
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--batch", type=int, default=B, help="sequences per GPU (profiling runs use fewer)")
+    ap.add_argument("--modes", default="f16,q8", help="KV modes to run (the first is the headline)")
+    ap.add_argument("--no-e2e", action="store_true")
     return ap.parse_args()
 
 
@@ -66,48 +67,53 @@ def peaks():
 
 
 class Clocks:
-    """nvidia-smi sampler running during the timed region."""
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-         "clocks_event_reasons.sw_power_cap")
+    """SM clock / throttle-reason sampler running during the timed region (NVML every 5 ms;
+    the same fields as the nvidia-smi clocks query)."""
+
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "sw_power_cap": 0x4}
 
     def __init__(self, index):
-        self.index = index
-        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        import threading
+        self.samples, self.err = [], None
+        self.stop_ev = threading.Event()
         try:
-            self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
-        except Exception:
-            self.p = None
+            import pynvml
+            pynvml.nvmlInit()
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            phys = int(vis.split(",")[index]) if vis and vis.split(",")[index].isdigit() else index
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(phys)
+            self.nv = pynvml
+            self.max = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # noqa: BLE001
+            self.err = f"nvml unavailable: {e}"
+            return
+        self.t = threading.Thread(target=self._run, daemon=True)
+        self.t.start()
+
+    def _run(self):
+        nv = self.nv
+        while not self.stop_ev.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.samples.append((sm, rs))
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(0.005)
 
     def stop(self):
-        if self.p is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.p.terminate()
-        try:
-            self.p.wait(timeout=5)
-        except Exception:
-            self.p.kill()
-        self.f.flush()
-        rows = []
-        for line in open(self.f.name):
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) >= 9:
-                rows.append(parts)
-        os.unlink(self.f.name)
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        reasons = set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            for n, v in zip(names, r[5:9]):
-                if v.strip().lower() == "active":
-                    reasons.add(n)
-        loaded = [s for s in sm if s > 0.5 * (max(mx) if mx else 1)] or sm
-        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": max(mx) if mx else None,
-                "samples": len(rows), "reasons": sorted(reasons)}
+        if self.err:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.err]}
+        self.stop_ev.set()
+        self.t.join(timeout=2)
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max, "reasons": ["no samples"]}
+        sm = [x[0] for x in self.samples]
+        reasons = sorted({n for _, r in self.samples for n, bit in self.REASONS.items() if r & bit})
+        loaded = [x for x in sm if x > 0.5 * self.max] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": self.max, "samples": len(sm),
+                "sm_mhz_min": min(sm), "reasons": reasons, "source": "nvml, 5 ms"}
 
 
 def make_cache(ops, torch, mode, seed, batch=B, ctx=L):
@@ -217,6 +223,19 @@ CONFIG = {"workload": "config 2: batched decode attention, Qwen3-8B shape (H32 K
           "parallelism": "batch-sharded, no communication"}
 
 
+def profiled_traffic(mode, batch):
+    """DRAM traffic per launch of the decode kernel from the committed ncu summary
+    (profiles/attn_tc_decode_<mode>.md, line `traffic_bytes_per_sequence = N`), scaled to `batch`
+    sequences (traffic grows linearly with the sequences a launch processes), or None."""
+    try:
+        for line in open(os.path.join(ROOT, "profiles", f"attn_tc_decode_{mode}.md")):
+            if line.strip().startswith("traffic_bytes_per_sequence"):
+                return int(float(line.split("=")[1].strip().split()[0]) * batch)
+    except OSError:
+        pass
+    return None
+
+
 def run_ours(args):
     import torch
     ws, rank, local = dist_env()
@@ -228,29 +247,38 @@ def run_ours(args):
     barrier = (lambda: dist.barrier()) if dist else (lambda: None)
     from bitgpu_b200 import ops
     hbm, _, peak_kind = peaks()
+    nb = args.batch
+    modes = [m for m in args.modes.split(",") if m]
 
-    q = torch.randn((B, 1, H, D), device="cuda", generator=torch.Generator(device="cuda").manual_seed(100 + rank))
+    def max_over_ranks(ms):
+        if not dist:
+            return ms
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    q = torch.randn((nb, 1, H, D), device="cuda", generator=torch.Generator(device="cuda").manual_seed(100 + rank))
     results = {}
-    for mode in ("f16", "q8"):
-        cache = make_cache(ops, torch, mode, seed=1000 * rank + (1 if mode == "f16" else 2))
-        out = torch.empty((B, 1, H, D), device="cuda")
+    for i, mode in enumerate(modes):
+        cache = make_cache(ops, torch, mode, seed=1000 * rank + i + 1, batch=nb)
+        out = torch.empty((nb, 1, H, D), device="cuda")
         fn = lambda: ops.attention(q, cache, L - 1, out=out)
-        clk = Clocks(local) if mode == "f16" else None
-        ms = time_steps(torch, fn, args.steps, args.warmup, barrier)
-        clocks = clk.stop() if clk else None
-        if dist:
-            t = torch.tensor([ms], device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        res = {"ms": ms, "gbs": alg_bytes(mode) * ws / (ms * 1e-3) / 1e9, "per_gpu_gbs": alg_bytes(mode) / (ms * 1e-3) / 1e9}
-        if mode == "f16":
-            res["clocks"] = clocks
-            # e2e through the public API: pinned host q + new K/V rows in, output back out, every step
-            qh = torch.randn((B, 1, H, D)).pin_memory()
-            kh = torch.randn((B, 1, KV, D)).pin_memory()
-            vh = torch.randn((B, 1, KV, D)).pin_memory()
-            oh = torch.empty((B, 1, H, D)).pin_memory()
-            qd, kd, vd = torch.empty_like(q), torch.empty((B, 1, KV, D), device="cuda"), torch.empty((B, 1, KV, D), device="cuda")
+        clk = Clocks(local) if i == 0 else None
+        ms = max_over_ranks(time_steps(torch, fn, args.steps, args.warmup, barrier))
+        ab = alg_bytes(mode, batch=nb)
+        res = {"ms": ms, "gbs": ab * ws / (ms * 1e-3) / 1e9, "per_gpu_gbs": ab / (ms * 1e-3) / 1e9, "bytes": ab}
+        if i == 0:
+            res["clocks"] = clk.stop()
+        if i == 0 and not args.no_e2e:
+            # e2e through the public API: pinned host q + the step's new K/V rows in, the attention
+            # output back out, every step (the cache itself stays resident, as in the engine)
+            qh = torch.randn((nb, 1, H, D)).pin_memory()
+            kh = torch.randn((nb, 1, KV, D)).pin_memory()
+            vh = torch.randn((nb, 1, KV, D)).pin_memory()
+            oh = torch.empty((nb, 1, H, D)).pin_memory()
+            qd = torch.empty_like(q)
+            kd = torch.empty((nb, 1, KV, D), device="cuda")
+            vd = torch.empty((nb, 1, KV, D), device="cuda")
 
             def e2e():
                 qd.copy_(qh, non_blocking=True)
@@ -260,14 +288,13 @@ def run_ours(args):
                 cache.append(1, vd, L - 1)
                 ops.attention(qd, cache, L - 1, out=out)
                 oh.copy_(out, non_blocking=True)
-            ms_e2e = time_steps(torch, e2e, args.steps, args.warmup, barrier)
-            if dist:
-                t = torch.tensor([ms_e2e], device="cuda")
-                dist.all_reduce(t, op=dist.ReduceOp.MAX)
-                ms_e2e = float(t.item())
-            res["e2e"] = {"value": round(alg_bytes(mode) * ws / (ms_e2e * 1e-3) / 1e9, 2), "unit": "GB/s",
-                          "h2d_bytes_per_step": qh.numel() * 4 + kh.numel() * 4 + vh.numel() * 4,
-                          "d2h_bytes_per_step": oh.numel() * 4, "ms_per_step": round(ms_e2e, 4)}
+                torch.cuda.current_stream().synchronize()
+                float(oh[0, 0, 0, 0])     # the host reads the step's result
+            ms_e2e = max_over_ranks(time_steps(torch, e2e, args.steps, args.warmup, barrier))
+            res["e2e"] = {"value": round(ab * ws / (ms_e2e * 1e-3) / 1e9, 2), "unit": "GB/s",
+                          "h2d_bytes_per_step": (qh.numel() + kh.numel() + vh.numel()) * 4,
+                          "d2h_bytes_per_step": oh.numel() * 4, "ms_per_step": round(ms_e2e, 4),
+                          "path": "bitgpu_b200.ops (ctypes -> libbgattn.so C ABI): bg_kv_append x2 + bg_attention"}
         results[mode] = res
         del cache
         torch.cuda.empty_cache()
@@ -276,28 +303,31 @@ def run_ours(args):
         if dist:
             dist.destroy_process_group()
         return
-    f16 = results["f16"]
-    per_launch_gbs = alg_bytes("f16") / (f16["ms"] * 1e-3) / 1e9
+    head = results[modes[0]]
+    per_launch = head["bytes"] / (head["ms"] * 1e-3) / 1e9
+    traffic = profiled_traffic(modes[0], nb)
     line = {
-        "metric": METRIC, "value": round(f16["gbs"], 2), "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(f16["ms"], 4), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f16", "data": "synthetic N(0,1), seeded; KV written through the library's "
-                                                    "own f16/q8 append",
-        "config": CONFIG,
-        "roofline": {"bound": "hbm", "achieved": round(per_launch_gbs, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(per_launch_gbs / hbm, 4), "peak_kind": peak_kind,
-                     "traffic": None,
-                     "note": "achieved = algorithmic bytes per launch (2*B*L*KV*256 + 2*B*H*D*4) / mean duration "
-                             "of one bg_attention call (split-KV kernel + LSE merge), CUDA events on its stream"},
-        "e2e": f16["e2e"],
+        "metric": METRIC, "value": round(head["gbs"], 2), "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(head["ms"], 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": modes[0],
+        "data": "synthetic N(0,1), seeded; KV written through the library's own f16/q8 append",
+        "config": dict(CONFIG, global_batch_per_gpu=nb, kv_mode=modes[0]),
+        "roofline": {"bound": "hbm", "achieved": round(per_launch, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(per_launch / hbm, 4), "peak_kind": f"{peak_kind} (copy, read+write)",
+                     "traffic": traffic, "algorithmic_bytes": head["bytes"],
+                     "note": "achieved = algorithmic bytes per launch (2*B*L*KV*rowB + 2*B*H*D*4) / mean duration "
+                             "of one bg_attention call (split-KV kernel + LSE merge), CUDA events on its stream; "
+                             "traffic = ncu dram read+write bytes per sequence (profiles/) x batch"},
         "gpu_launches": 2 * args.steps,
-        "clocks": f16["clocks"],
-        "variants": {"q8": {"value": round(results["q8"]["gbs"], 2), "unit": "GB/s", "ms_per_step": round(results["q8"]["ms"], 4),
-                            "frac": round(results["q8"]["per_gpu_gbs"] / hbm, 4),
-                            "bytes_per_step_per_gpu": alg_bytes("q8")}},
+        "clocks": head["clocks"],
+        "variants": {m: {"value": round(r["gbs"], 2), "unit": "GB/s", "ms_per_step": round(r["ms"], 4),
+                         "frac": round(r["per_gpu_gbs"] / hbm, 4), "bytes_per_step_per_gpu": r["bytes"]}
+                     for m, r in results.items() if m != modes[0]},
     }
+    if "e2e" in head:
+        line["e2e"] = head["e2e"]
     if ws == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline("f16", args.cpu_seconds)
+        line["cpu_baseline"] = cpu_baseline(modes[0], args.cpu_seconds)
     print(json.dumps(line), flush=True)
     if dist:
         dist.destroy_process_group()

@@ -15,7 +15,7 @@ DT_F32, DT_F16 = 0, 1
 
 # every symbol include/bgattn.h declares (checked by the CPU test suite)
 EXPORTS = [
-    "bg_strerror", "bg_version", "bg_attention_workspace_size", "bg_attention", "bg_attention_partials",
+    "bg_strerror", "bg_version", "bg_device_status", "bg_force_generic", "bg_attention_workspace_size", "bg_attention", "bg_attention_partials",
     "bg_lse_merge", "bg_kv_append", "bg_rmsnorm_rope", "bg_kv_evict", "bg_kv_ring_evict",
     "bg_deltanet_gbeta", "bg_deltanet_recur", "bg_deltanet_norm_gate", "bg_deltanet_fused",
     "bg_gate_sigmoid", "bg_attention_noalloc",
@@ -45,6 +45,8 @@ P, U32, U64, F, SZ = C.c_void_p, C.c_uint32, C.c_uint64, C.c_float, C.c_size_t
 _SIGS = {
     "bg_strerror": (C.c_char_p, [C.c_int]),
     "bg_version": (C.c_int, []),
+    "bg_device_status": (C.c_int, [P]),
+    "bg_force_generic": (C.c_int, [C.c_int]),
     "bg_attention_workspace_size": (SZ, [C.POINTER(AttnParams), U32]),
     "bg_attention": (C.c_int, [C.POINTER(AttnParams), U32, P, U32, C.POINTER(KVCacheDesc), P, P, F, P, P, U32, P,
                                SZ, P]),

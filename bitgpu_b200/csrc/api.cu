@@ -1,6 +1,7 @@
 // extern "C" entry points of libbgattn.so: argument validation (mirroring the engine's
 // validation throws) and dispatch to the sm_100a kernels.  See include/bgattn.h.
 #include <math.h>
+#include <stdlib.h>
 
 #include "attn.h"
 #include "kv.h"
@@ -8,6 +9,8 @@
 using namespace bg;
 
 namespace {
+
+int g_force_generic = 0;  // bg_force_generic (the reference's forceNoSubgroups analogue)
 
 bool kv_mode_ok(uint32_t m) { return m <= BG_KV_Q8R; }
 
@@ -71,11 +74,17 @@ int run_attention(const bg_attn_params *p, uint32_t batch, const void *q, uint32
   a.pos_hi = pos_hi;
   const uint64_t rows = (uint64_t)batch * p->S * p->H;
   const uint32_t L = pos_hi > pos_lo ? pos_hi - pos_lo : 1;
-  a.nsplit = attn_num_splits(batch, p->S, p->H, p->KV, p->D, L);
-  a.chunk = (L + a.nsplit - 1) / a.nsplit;
+  const bool tc = !g_force_generic && attn_tc_supported(a.mode, p->D, p->S, p->H, p->KV, cosT != nullptr,
+                                                        kv->window != 0);
+  a.nsplit = attn_num_splits(batch, p->S, p->H, p->KV, p->D, L, a.mode, tc);
+  if (const char *ov = getenv("BGATTN_NSPLIT")) {  // tuning sweeps only; bounded by the workspace sizing
+    const uint32_t n = (uint32_t)atoi(ov), mx = attn_max_splits(batch, p->S, p->H, p->KV, p->D, L);
+    if (n >= 1) a.nsplit = n < mx ? n : mx;
+  }
+  a.chunk = ((L + a.nsplit - 1) / a.nsplit + 63) / 64 * 64;  // whole 64-position tiles
   if (ws_bytes < part_bytes(a.nsplit, rows, p->D) || (!ws && rows)) return BG_ENOMEM;
   a.partials = static_cast<float *>(ws);
-  int rc = launch_attn_tc(a, st);
+  int rc = tc ? launch_attn_tc(a, st) : BG_EUNSUPPORTED;
   if (rc == BG_EUNSUPPORTED) rc = launch_attn_generic(a, st);
   if (rc) return rc;
   if (partials_out) return launch_lse_merge(a.partials, a.nsplit, (uint32_t)rows, p->D, nullptr, partials_out, -1, st);
@@ -100,10 +109,22 @@ const char *bg_strerror(int code) {
 
 int bg_version(void) { return 1; }
 
+int bg_force_generic(int on) {
+  const int prev = g_force_generic;
+  g_force_generic = on ? 1 : 0;
+  return prev;
+}
+
+int bg_device_status(bg_stream_t stream) {
+  if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return BG_ELAUNCH;
+  int e = poll_device_error_attn_tc();
+  return e ? (e < 0 ? e : BG_ELAUNCH) : BG_OK;
+}
+
 size_t bg_attention_workspace_size(const bg_attn_params *p, uint32_t batch) {
   if (!p || !p->KV || !p->H) return 0;
   const uint32_t L = p->Ltot ? p->Ltot : 1;
-  const uint32_t ns = attn_num_splits(batch, p->S, p->H, p->KV, p->D, L);
+  const uint32_t ns = attn_max_splits(batch, p->S, p->H, p->KV, p->D, L);
   return part_bytes(ns, (uint64_t)batch * p->S * p->H, p->D);
 }
 

@@ -17,13 +17,21 @@ struct AttnArgs {
   uint32_t nsplit, chunk;    // split j covers [pos_lo + j*chunk, pos_lo + (j+1)*chunk)
 };
 
-// Number of KV splits used for a full attention call; the workspace holds
-// nsplit * B*S*H * (D+2) floats.
-uint32_t attn_num_splits(uint32_t B, uint32_t S, uint32_t H, uint32_t KV, uint32_t D, uint32_t L);
+// Number of KV splits for one attention call over L positions with the given cache mode and
+// kernel (tensor-core or not); the workspace holds nsplit * B*S*H * (D+2) floats.
+// attn_max_splits is the maximum over every mode/kernel (what workspace sizing reserves).
+uint32_t attn_num_splits(uint32_t B, uint32_t S, uint32_t H, uint32_t KV, uint32_t D, uint32_t L, int mode, bool tc);
+uint32_t attn_max_splits(uint32_t B, uint32_t S, uint32_t H, uint32_t KV, uint32_t D, uint32_t L);
+bool attn_tc_supported(int mode, uint32_t D, uint32_t S, uint32_t H, uint32_t KV, bool roll, bool ring);
+int attn_tc_ctas_per_sm(int mode, uint32_t D, uint32_t M);
+int attn_generic_ctas_per_sm(int mode, uint32_t D, uint32_t rows, bool roll);
 
 int launch_attn_generic(const AttnArgs &a, cudaStream_t st);
 int launch_attn_tc(const AttnArgs &a, cudaStream_t st);  // returns BG_EUNSUPPORTED if not covered
 int launch_lse_merge(const float *partials, uint32_t nsplit, uint32_t rows, uint32_t D,
                      const float *gate, void *out, int out_f16, cudaStream_t st);
+
+// Read-and-clear the bounded-wait timeout flag of the TMA kernels (BG_ETIMEOUT or 0).
+int poll_device_error_attn_tc();
 
 }  // namespace bg

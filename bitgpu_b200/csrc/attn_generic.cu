@@ -252,18 +252,109 @@ int launch_d(const AttnArgs &a, cudaStream_t st) {
 
 }  // namespace
 
-uint32_t attn_num_splits(uint32_t B, uint32_t S, uint32_t H, uint32_t KV, uint32_t D, uint32_t L) {
-  // Enough CTAs to cover 148 SMs a few times over, but never a split shorter than 64
-  // positions (each split costs a partial row write + merge read).
+namespace {
+
+template <int MODE, int D, bool ROLL, int RB>
+int generic_occ() {
+  static int cached = 0;
+  if (!cached) {
+    int n = 0;
+    const int smem = 4 * RB * (D + 2) * (int)sizeof(float);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, attn_generic_kernel<MODE, D, ROLL, RB>, 128, smem) !=
+            cudaSuccess ||
+        n < 1)
+      n = 1;
+    cached = n;
+  }
+  return cached;
+}
+
+template <int MODE, int D>
+int generic_occ_rb(uint32_t rows, bool roll) {
+  constexpr int RBMAX = D >= 256 ? 4 : 8;
+  auto pick = [&](auto rbc) -> int {
+    constexpr int RB = decltype(rbc)::value;
+    return roll ? generic_occ<MODE, D, true, RB>() : generic_occ<MODE, D, false, RB>();
+  };
+  if (rows <= 1) return pick(std::integral_constant<int, 1>{});
+  if (rows <= 2) return pick(std::integral_constant<int, 2>{});
+  if (rows <= 4 || RBMAX == 4) return pick(std::integral_constant<int, (RBMAX < 4 ? RBMAX : 4)>{});
+  return pick(std::integral_constant<int, RBMAX>{});
+}
+
+template <int MODE>
+int generic_occ_d(uint32_t D, uint32_t rows, bool roll) {
+  switch (D) {
+    case 64: return generic_occ_rb<MODE, 64>(rows, roll);
+    case 128: return generic_occ_rb<MODE, 128>(rows, roll);
+    default: return generic_occ_rb<MODE, 256>(rows, roll);
+  }
+}
+
+uint32_t kv_row_bytes(int mode, uint32_t D) {
+  switch (mode) {
+    case BG_KV_F32: return 4 * D;
+    case BG_KV_F16: return 2 * D;
+    case BG_KV_Q8: return D + D / 8;
+    default: return D + D / 32;
+  }
+}
+
+}  // namespace
+
+int attn_generic_ctas_per_sm(int mode, uint32_t D, uint32_t rows, bool roll) {
+  switch (mode) {
+    case BG_KV_F32: return generic_occ_d<BG_KV_F32>(D, rows, roll);
+    case BG_KV_F16: return generic_occ_d<BG_KV_F16>(D, rows, roll);
+    case BG_KV_Q8: return generic_occ_d<BG_KV_Q8>(D, rows, roll);
+    default: return D % 128 ? 1 : generic_occ_d<BG_KV_Q8R>(D, rows, roll);
+  }
+}
+
+// Split count from a small cost model in units of bytes moved at full HBM rate:
+//   waves(n) * slots * (bytes of one CTA's slice + pipeline ramp)  +  n * partial-row traffic,
+// where a CTA's slice is the unit's cache bytes / n and `slots` = resident CTAs on 148 SMs.
+// The first term rewards filling the last wave; the second charges the split partials'
+// write + merge read.  Splits never get shorter than 256 positions.
+uint32_t attn_num_splits(uint32_t B, uint32_t S, uint32_t H, uint32_t KV, uint32_t D, uint32_t L, int mode, bool tc) {
   const uint32_t G = H / KV;
+  const uint32_t M = S * G;
   const uint32_t rb = D >= 256 ? 4 : 8;
-  const uint64_t base = (uint64_t)B * KV * ((S * G + rb - 1) / rb);
-  const uint64_t want = (4 * 148 + base - 1) / base;
-  const uint64_t maxs = (L + 63) / 64;
-  uint64_t n = want < maxs ? want : maxs;
-  if (n < 1) n = 1;
-  if (n > 256) n = 256;
-  return (uint32_t)n;
+  const uint64_t rowchunks = tc ? 1 : (M + rb - 1) / rb;
+  const uint64_t units = (uint64_t)B * KV * rowchunks;
+  const int per_sm = tc ? attn_tc_ctas_per_sm(mode, D, M) : attn_generic_ctas_per_sm(mode, D, M, false);
+  const double slots = 148.0 * per_sm;
+  const double unit_bytes = 2.0 * L * kv_row_bytes(mode, D);
+  const double ramp = 2.0 * 64 * 2 * kv_row_bytes(mode, D);
+  const double split_bytes = (double)B * S * H * (D + 2) * 8.0;
+  uint64_t maxs = (L + 255) / 256;
+  if (maxs > 128) maxs = 128;
+  if (maxs < 1) maxs = 1;
+  uint32_t best = 1;
+  double best_cost = 0;
+  for (uint64_t n = 1; n <= maxs; ++n) {
+    const double waves = (double)((units * n + (uint64_t)slots - 1) / (uint64_t)slots);
+    const double cost = waves * slots * (unit_bytes / n + ramp) + n * split_bytes;
+    if (n == 1 || cost < best_cost * 0.999) {
+      best = (uint32_t)n;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
+
+uint32_t attn_max_splits(uint32_t B, uint32_t S, uint32_t H, uint32_t KV, uint32_t D, uint32_t L) {
+  uint32_t m = 1;
+  for (int mode = BG_KV_F32; mode <= BG_KV_Q8R; ++mode) {
+    if (mode == BG_KV_Q8R && D % 128) continue;
+    const uint32_t a = attn_num_splits(B, S, H, KV, D, L, mode, false);
+    m = a > m ? a : m;
+    if (attn_tc_supported(mode, D, S, H, KV, false, false)) {
+      const uint32_t t = attn_num_splits(B, S, H, KV, D, L, mode, true);
+      m = t > m ? t : m;
+    }
+  }
+  return m;
 }
 
 int launch_attn_generic(const AttnArgs &a, cudaStream_t st) {

@@ -1,6 +1,583 @@
-// Tensor-core split-KV decode for f16 / q8 caches (filled in by the tcgen05/mma kernels).
+// Tensor-core split-KV decode attention for f16 and q8 KV caches (sm_100a).
+//
+// Decode attention is HBM-bound: every cached K/V row is read once per step and the math per row
+// is tiny.  The design keeps HBM busy and keeps the per-row math off the issue-bound CUDA-core
+// path:
+//   * one producer warp streams K/V tiles of 64 positions for one (sequence, kv head) into shared
+//     memory with 4-D TMA tiled loads (128-byte swizzle, no multicast), through an NST-deep
+//     mbarrier ring;
+//   * four consumer warps each own 16 positions of a tile.  Scores are computed transposed,
+//     S^T = K . Q^T (m16n8k16: positions on M, the GQA group's query rows on N, head_dim on K),
+//     so the <= 8 query rows of a group pad only N to 8.  Q (f32) is split hi + lo into two f16
+//     operands, so scores keep ~22 bits although K is f16 (or int8 codes);
+//   * the output is accumulated transposed too, O^T = V^T . P^T (head_dim on M, rows on N).  The
+//     score accumulator of a warp is converted to the P^T operand in registers with movmatrix;
+//   * q8: codes enter the MMA as exact f16 integers.  The K block scale (one per 32 values) is
+//     applied per block accumulator after the MMA, and the V block scale is folded into P before
+//     its f16 conversion, so the q8 math stays exact up to f32/f16 operand rounding of q and p.
+// Online softmax in log2 units; the four warps' states are merged in shared memory and written as
+// split partials [split][row][D+2] for the LSE merge kernel (shared with the generic path).
+#include <cuda.h>
+#include <cuda_fp16.h>
+
 #include "attn.h"
+#include "tma.cuh"
 
 namespace bg {
-int launch_attn_tc(const AttnArgs &, cudaStream_t) { return BG_EUNSUPPORTED; }
+namespace {
+
+struct TcParams {
+  const void *q;
+  int q_f16;
+  float *partials;
+  uint32_t B, S, H, KV, G, M;
+  uint32_t posBase, pos_lo, pos_hi, chunk, row_offset;
+  uint32_t nrows_total;
+  float sl2;  // softmax scale * log2(e)
+};
+
+template <int MODE, int D>
+struct Cfg {
+  static constexpr int ES = MODE == BG_KV_F16 ? 2 : 1;
+  static constexpr int TP = 64;   // positions per tile
+  static constexpr int NCW = 4;   // consumer warps, 16 positions each
+  static constexpr int ROWB = D * ES;
+  static constexpr int NCB = ROWB / 128;       // 128-byte column blocks per row
+  static constexpr int KVT = TP * ROWB;        // bytes of the K (or V) tile
+  static constexpr int NB = D / 32;            // q8 blocks per row
+  static constexpr int SCT = MODE == BG_KV_Q8 ? TP * NB * 4 : 0;
+  static constexpr int STAGE = 2 * KVT + 2 * SCT;
+  // q8 tiles are half the bytes of f16 ones but need more issue slots per byte: a smaller ring
+  // (72 KB) lets 3 CTAs share an SM; f16 keeps 96 KB rings at 2 CTAs per SM.
+  static constexpr int NST_RAW = (MODE == BG_KV_Q8 ? 73728 : 98304) / STAGE;
+  static constexpr int NST = NST_RAW < 2 ? 2 : (NST_RAW > 6 ? 6 : NST_RAW);
+  static constexpr int SMEM = NST * STAGE + 1024 /*align*/ + 2 * NST * 8 /*barriers*/ + 16 * NB * 4 /*q8 seeds*/;
+};
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t movm_t(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
+__device__ __forceinline__ uint32_t pack_f16(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+
+// Two int8 codes of `w` (bytes picked by `sel`, see __byte_perm) -> exact f16x2.
+// 0x64XX as f16 is 1024 + XX; the codes are biased by 128 first, so subtract 1152.
+__device__ __forceinline__ uint32_t i8pair_f16(uint32_t w, uint32_t sel) {
+  const uint32_t r = __byte_perm(w ^ 0x80808080u, 0x64646464u, sel);
+  __half2 h = *reinterpret_cast<const __half2 *>(&r);
+  h = __hsub2(h, __half2(__float2half_rn(1152.f), __float2half_rn(1152.f)));
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+constexpr uint32_t kSelLo = 0x4140, kSelHi = 0x4342, kSelEven = 0x4240, kSelOdd = 0x4341;
+
+// Biased form without the subtraction: (code + 1152) as exact f16x2, from a word already xored
+// with 0x80808080.  The kernels remove the +1152 inside the MMA instead (accumulator seed for K,
+// an extra MMA with a constant -1152 operand for V).
+__device__ __forceinline__ uint32_t i8pair_biased(uint32_t wx, uint32_t sel) {
+  return __byte_perm(wx, 0x64646464u, sel);
+}
+__device__ __forceinline__ uint32_t kNeg1152x2() {
+  __half2 h = __half2(__float2half_rn(-1152.f), __float2half_rn(-1152.f));
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+
+// Shared-memory byte address of 16-byte chunk `gc` of tile row `row` (128B-swizzled column blocks
+// of TP rows each, the layout TMA writes with CU_TENSOR_MAP_SWIZZLE_128B).
+template <int TP>
+__device__ __forceinline__ uint32_t swz(uint32_t base, int row, int gc) {
+  return base + (gc >> 3) * (TP * 128) + row * 128 + (((gc & 7) ^ (row & 7)) << 4);
+}
+
+template <int MODE, int D, int NT>
+__global__ void __launch_bounds__(160, (MODE == BG_KV_Q8 && NT == 1 && D == 128) ? 3 : 1) attn_tc_kernel(const __grid_constant__ CUtensorMap tmK,
+                                                      const __grid_constant__ CUtensorMap tmV,
+                                                      const __grid_constant__ CUtensorMap tmKs,
+                                                      const __grid_constant__ CUtensorMap tmVs, TcParams p) {
+  using C = Cfg<MODE, D>;
+  constexpr int TP = C::TP, NST = C::NST, NB = C::NB;
+  constexpr int KS = D / 16;  // 16-wide k steps over head_dim
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + NST * C::STAGE);
+  uint64_t *empty = full + NST;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t split = blockIdx.x;
+  const uint32_t b = blockIdx.y / p.KV, kvh = blockIdx.y % p.KV;
+  const uint32_t lo = p.pos_lo + split * p.chunk;
+  uint32_t hi = min(p.pos_hi, lo + p.chunk);
+  hi = min(hi, p.posBase + p.S);
+  const int ntiles = hi > lo ? (int)((hi - lo + TP - 1) / TP) : 0;
+
+  if (tid == 0) {
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], C::NCW);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == C::NCW) {  // ---------------- producer warp ----------------
+    if (lane == 0 && ntiles > 0) {
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmV);
+      if constexpr (MODE == BG_KV_Q8) {
+        prefetch_tmap(&tmKs);
+        prefetch_tmap(&tmVs);
+      }
+      bool ok = true;
+      for (int t = 0; t < ntiles && ok; ++t) {
+        const int s = t % NST;
+        if (t >= NST) ok = mbar_wait(&empty[s], ((t / NST) - 1) & 1);
+        if (!ok) break;
+        unsigned char *st = smem + s * C::STAGE;
+        mbar_expect_tx(&full[s], C::STAGE);
+        const int z = (int)(lo + t * TP - p.row_offset);
+#pragma unroll
+        for (int cb = 0; cb < C::NCB; ++cb) {
+          tma_load_4d(st + cb * TP * 128, &tmK, &full[s], cb * (128 / C::ES), (int)kvh, z, (int)b);
+          tma_load_4d(st + C::KVT + cb * TP * 128, &tmV, &full[s], cb * (128 / C::ES), (int)kvh, z, (int)b);
+        }
+        if constexpr (MODE == BG_KV_Q8) {
+          tma_load_4d(st + 2 * C::KVT, &tmKs, &full[s], 0, (int)kvh, z, (int)b);
+          tma_load_4d(st + 2 * C::KVT + C::SCT, &tmVs, &full[s], 0, (int)kvh, z, (int)b);
+        }
+      }
+      // never leave the CTA with bulk copies in flight: wait (bounded) for the last loads
+      for (int t = max(0, ntiles - NST); t < ntiles; ++t) mbar_wait(&full[t % NST], (t / NST) & 1);
+    }
+    return;
+  }
+
+  // ---------------- consumer warps ----------------
+  // Q^T operand fragments (B of m16n8k16): column n = lane/4 (query row of the group), k pairs.
+  uint32_t qh[NT][KS][2], ql[NT][KS][2];
+  uint32_t lim[NT][2];  // last attended position of the lane's two score columns
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const uint32_t r = nt * 8 + (lane >> 2);
+    const bool rv = r < p.M;
+    const uint32_t qi = rv ? r / p.G : 0, h = kvh * p.G + (rv ? r % p.G : 0);
+    const uint64_t qoff = (((uint64_t)b * p.S + qi) * p.H + h) * D;
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        // f16 cache: k slots 2j,2j+1 (+8) <-> dims 2j,2j+1 (+8); q8 cache: the byte-pair order of
+        // the int8 fragments, dims 4j,4j+1 (half 0) and 4j+2,4j+3 (half 1), j = lane % 4.
+        const int d = MODE == BG_KV_Q8 ? ks * 16 + 4 * (lane & 3) + 2 * half : ks * 16 + 2 * (lane & 3) + 8 * half;
+        float x0 = 0.f, x1 = 0.f;
+        if (rv) {
+          if (p.q_f16) {
+            const __half *qp = static_cast<const __half *>(p.q) + qoff + d;
+            x0 = __half2float(qp[0]);
+            x1 = __half2float(qp[1]);
+          } else {
+            const float2 v = *reinterpret_cast<const float2 *>(static_cast<const float *>(p.q) + qoff + d);
+            x0 = v.x;
+            x1 = v.y;
+          }
+        }
+        const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
+        qh[nt][ks][half] = pack_f16(__half2float(h0), __half2float(h1));
+        ql[nt][ks][half] = pack_f16(x0 - __half2float(h0), x1 - __half2float(h1));
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const uint32_t rc = nt * 8 + 2 * (lane & 3) + j;
+      lim[nt][j] = p.posBase + (rc < p.M ? rc / p.G : p.S - 1);
+    }
+  }
+
+  // q8: the K accumulators start at -1152 * sum(q over the 32-value block) of their score column,
+  // which cancels the +1152 bias of the codes fed to the MMA.  Seeds live in shared memory
+  // ([column][block], after the barriers) to keep registers for occupancy.
+  float *kcorr_s = reinterpret_cast<float *>(empty + NST);
+  if constexpr (MODE == BG_KV_Q8) {
+    for (int idx = tid; idx < NT * 8 * NB; idx += C::NCW * 32) {
+      const uint32_t rc = idx / NB, bk = idx % NB;
+      float sum = 0.f;
+      if (rc < p.M) {
+        const uint32_t qi = rc / p.G, h = kvh * p.G + rc % p.G;
+        const uint64_t qoff = (((uint64_t)b * p.S + qi) * p.H + h) * D + bk * 32;
+        for (int d = 0; d < 32; ++d) {
+          const float x = p.q_f16 ? __half2float(static_cast<const __half *>(p.q)[qoff + d])
+                                  : static_cast<const float *>(p.q)[qoff + d];
+          const float hi = __half2float(__float2half_rn(x));
+          sum += hi + __half2float(__float2half_rn(x - hi));
+        }
+      }
+      kcorr_s[idx] = -1152.f * sum;
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+  }
+
+  float m[NT][2], l[NT][2];
+  float oacc[NT][KS][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    m[nt][0] = m[nt][1] = kNegBig;
+    l[nt][0] = l[nt][1] = 0.f;
+#pragma unroll
+    for (int mt = 0; mt < KS; ++mt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) oacc[nt][mt][i] = 0.f;
+  }
+
+  const int lrow = (((lane >> 3) & 1) << 3) + (lane & 7);  // ldmatrix row for matrices {0,1},{2,3}
+  const int lhi = lane >> 4;
+  const int trow = ((lane >> 4) << 3) + (lane & 7);         // .trans f16 V: matrices (pos, d) order
+  const int tcol = (lane >> 3) & 1;
+  bool ok = true;
+  for (int t = 0; t < ntiles; ++t) {
+    const int s = t % NST;
+    if (!mbar_wait(&full[s], (t / NST) & 1)) {
+      ok = false;
+      break;
+    }
+    const uint32_t sb = smem_u32(smem + s * C::STAGE);
+    const uint32_t kb = sb, vb = sb + C::KVT;
+    const int row0 = warp * 16;
+    const uint32_t pa = lo + t * TP + row0 + (lane >> 2), pb = pa + 8;
+
+    // ---- scores S^T[pos][n] ----
+    float sc[NT][4];
+    if constexpr (MODE == BG_KV_F16) {
+      float acc[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[nt][i] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+        uint32_t a[4];
+        ldsm_x4(a, swz<TP>(kb, row0 + lrow, 2 * ks + lhi));
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          mma16816(acc[nt], a, qh[nt][ks][0], qh[nt][ks][1]);
+          mma16816(acc[nt], a, ql[nt][ks][0], ql[nt][ks][1]);
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sc[nt][i] = acc[nt][i] * p.sl2;
+    } else {
+      const float *ksc = reinterpret_cast<const float *>(smem + s * C::STAGE + 2 * C::KVT);
+      float acc[NT][NB][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int bk = 0; bk < NB; ++bk)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[nt][bk][i] = kcorr_s[(nt * 8 + 2 * (lane & 3) + (i & 1)) * NB + bk];
+#pragma unroll
+      for (int bk = 0; bk < NB; ++bk) {
+        uint32_t r[4];
+        ldsm_x4(r, swz<TP>(kb, row0 + lrow, 2 * bk + lhi));
+#pragma unroll
+        for (int i = 0; i < 4; ++i) r[i] ^= 0x80808080u;
+        const uint32_t a0[4] = {i8pair_biased(r[0], kSelLo), i8pair_biased(r[1], kSelLo),
+                                i8pair_biased(r[0], kSelHi), i8pair_biased(r[1], kSelHi)};
+        const uint32_t a1[4] = {i8pair_biased(r[2], kSelLo), i8pair_biased(r[3], kSelLo),
+                                i8pair_biased(r[2], kSelHi), i8pair_biased(r[3], kSelHi)};
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          mma16816(acc[nt][bk], a0, qh[nt][2 * bk][0], qh[nt][2 * bk][1]);
+          mma16816(acc[nt][bk], a0, ql[nt][2 * bk][0], ql[nt][2 * bk][1]);
+          mma16816(acc[nt][bk], a1, qh[nt][2 * bk + 1][0], qh[nt][2 * bk + 1][1]);
+          mma16816(acc[nt][bk], a1, ql[nt][2 * bk + 1][0], ql[nt][2 * bk + 1][1]);
+        }
+      }
+      float sa[NB], sbv[NB];
+#pragma unroll
+      for (int bk = 0; bk < NB; ++bk) {
+        sa[bk] = ksc[(row0 + (lane >> 2)) * NB + bk] * (p.sl2 * (1.0f / 127.0f));
+        sbv[bk] = ksc[(row0 + (lane >> 2) + 8) * NB + bk] * (p.sl2 * (1.0f / 127.0f));
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+        for (int bk = 0; bk < NB; ++bk) {
+          s0 = fmaf(acc[nt][bk][0], sa[bk], s0);
+          s1 = fmaf(acc[nt][bk][1], sa[bk], s1);
+          s2 = fmaf(acc[nt][bk][2], sbv[bk], s2);
+          s3 = fmaf(acc[nt][bk][3], sbv[bk], s3);
+        }
+        sc[nt][0] = s0;
+        sc[nt][1] = s1;
+        sc[nt][2] = s2;
+        sc[nt][3] = s3;
+      }
+    }
+
+    // ---- online softmax (columns n0 = 2(lane%4), n1 = n0+1; rows pa, pb) ----
+    float pr[NT][4], cr[NT][2];
+    bool moved = false;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        float x0 = (pa < hi && pa <= lim[nt][j]) ? sc[nt][j] : -INFINITY;
+        float x1 = (pb < hi && pb <= lim[nt][j]) ? sc[nt][2 + j] : -INFINITY;
+        float mx = fmaxf(x0, x1);
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        const float mn = fmaxf(m[nt][j], mx);
+        const float corr = exp2f(m[nt][j] - mn);
+        const float p0 = exp2f(x0 - mn), p1 = exp2f(x1 - mn);
+        l[nt][j] = l[nt][j] * corr + p0 + p1;
+        m[nt][j] = mn;
+        pr[nt][j] = p0;
+        pr[nt][2 + j] = p1;
+        cr[nt][j] = corr;
+        moved |= corr != 1.0f;
+      }
+    }
+    // rescale the output only when some running max of this warp moved (rare after the first
+    // tiles of a long context)
+    if (__any_sync(0xffffffffu, moved)) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int mt = 0; mt < KS; ++mt)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) oacc[nt][mt][i] *= cr[nt][i & 1];
+    }
+
+    // ---- O^T += V^T . P^T ----
+    if constexpr (MODE == BG_KV_F16) {
+      uint32_t pb0[NT], pb1[NT];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        pb0[nt] = movm_t(pack_f16(pr[nt][0], pr[nt][1]));
+        pb1[nt] = movm_t(pack_f16(pr[nt][2], pr[nt][3]));
+      }
+#pragma unroll
+      for (int mt = 0; mt < KS; ++mt) {
+        uint32_t a[4];
+        ldsm_x4_t(a, swz<TP>(vb, row0 + trow, 2 * mt + tcol));
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma16816(oacc[nt][mt], a, pb0[nt], pb1[nt]);
+      }
+    } else {
+      const float *vsc = reinterpret_cast<const float *>(smem + s * C::STAGE + 2 * C::KVT + C::SCT);
+#pragma unroll
+      for (int bk = 0; bk < NB; ++bk) {
+        const float va = vsc[(row0 + (lane >> 2)) * NB + bk] * (1.0f / 127.0f);
+        const float vbb = vsc[(row0 + (lane >> 2) + 8) * NB + bk] * (1.0f / 127.0f);
+        uint32_t pb0[NT], pb1[NT];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          pb0[nt] = movm_t(pack_f16(pr[nt][0] * va, pr[nt][1] * va));
+          pb1[nt] = movm_t(pack_f16(pr[nt][2] * vbb, pr[nt][3] * vbb));
+        }
+        uint32_t r[4];
+        ldsm_x4_t(r, swz<TP>(vb, row0 + lrow, 2 * bk + lhi));
+#pragma unroll
+        for (int i = 0; i < 4; ++i) r[i] ^= 0x80808080u;
+        const uint32_t a0[4] = {i8pair_biased(r[0], kSelEven), i8pair_biased(r[0], kSelOdd),
+                                i8pair_biased(r[1], kSelEven), i8pair_biased(r[1], kSelOdd)};
+        const uint32_t a1[4] = {i8pair_biased(r[2], kSelEven), i8pair_biased(r[2], kSelOdd),
+                                i8pair_biased(r[3], kSelEven), i8pair_biased(r[3], kSelOdd)};
+        const uint32_t ng = kNeg1152x2();
+        const uint32_t aneg[4] = {ng, ng, ng, ng};
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          mma16816(oacc[nt][2 * bk], a0, pb0[nt], pb1[nt]);
+          mma16816(oacc[nt][2 * bk], aneg, pb0[nt], pb1[nt]);
+          mma16816(oacc[nt][2 * bk + 1], a1, pb0[nt], pb1[nt]);
+          mma16816(oacc[nt][2 * bk + 1], aneg, pb0[nt], pb1[nt]);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+
+  // ---- merge the four warps' states; write split partials ----
+  constexpr int NN = NT * 8;
+  asm volatile("bar.sync 1, 128;" ::: "memory");  // all consumers done with the stages
+  float *ep = reinterpret_cast<float *>(smem);     // [NCW][NN][D+2]
+  float *mine = ep + warp * NN * (D + 2);
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      float lt = l[nt][j];
+      lt += __shfl_xor_sync(0xffffffffu, lt, 4);
+      lt += __shfl_xor_sync(0xffffffffu, lt, 8);
+      lt += __shfl_xor_sync(0xffffffffu, lt, 16);
+      const int n = nt * 8 + 2 * (lane & 3) + j;
+      if (lane < 4) {
+        mine[n * (D + 2) + D] = ok ? m[nt][j] : kNegBig;
+        mine[n * (D + 2) + D + 1] = ok ? lt : 0.f;
+      }
+#pragma unroll
+      for (int mt = 0; mt < KS; ++mt) {
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int d = MODE == BG_KV_F16 ? mt * 16 + (lane >> 2) + 8 * hh : mt * 16 + 2 * (lane >> 2) + hh;
+          mine[n * (D + 2) + d] = oacc[nt][mt][2 * hh + j];
+        }
+      }
+    }
+  }
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  for (int idx = tid; idx < (int)p.M * D; idx += C::NCW * 32) {
+    const int n = idx / D, d = idx % D;
+    float M = kNegBig;
+#pragma unroll
+    for (int w = 0; w < C::NCW; ++w) M = fmaxf(M, ep[(w * NN + n) * (D + 2) + D]);
+    float o = 0.f, L = 0.f;
+#pragma unroll
+    for (int w = 0; w < C::NCW; ++w) {
+      const float *st = ep + (w * NN + n) * (D + 2);
+      const float f = exp2f(st[D] - M);
+      o = fmaf(st[d], f, o);
+      L = fmaf(st[D + 1], f, L);
+    }
+    const uint32_t qi = n / p.G, h = kvh * p.G + n % p.G;
+    const uint64_t grow = ((uint64_t)b * p.S + qi) * p.H + h;
+    float *dst = p.partials + ((uint64_t)split * p.nrows_total + grow) * (D + 2);
+    dst[d] = o;
+    if (d == 0) {
+      dst[D] = L > 0.f ? M * kLn2 : -INFINITY;
+      dst[D + 1] = L;
+    }
+  }
+}
+
+template <int MODE, int D, int NT>
+int launch_cfg(const AttnArgs &a, cudaStream_t st) {
+  using C = Cfg<MODE, D>;
+  CUtensorMap tk, tv, tks, tvs;
+  const uint64_t Lvalid = a.pos_hi - a.kv.row_offset;
+  const uint64_t dims[4] = {a.D, a.KV, Lvalid, a.B};
+  const uint64_t rb = (uint64_t)a.D * C::ES;
+  const uint64_t strides[3] = {rb, rb * a.KV, rb * a.KV * a.kv.seq_stride};
+  const uint32_t box[4] = {128 / C::ES, 1, C::TP, 1};
+  const CUtensorMapDataType dt = MODE == BG_KV_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  if (make_tmap_4d(&tk, dt, a.kv.K, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) return BG_EUNSUPPORTED;
+  if (make_tmap_4d(&tv, dt, a.kv.V, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) return BG_EUNSUPPORTED;
+  if constexpr (MODE == BG_KV_Q8) {
+    const uint64_t sd[4] = {C::NB, a.KV, Lvalid, a.B};
+    const uint64_t sr = (uint64_t)C::NB * 4;
+    const uint64_t ss[3] = {sr, sr * a.KV, sr * a.KV * a.kv.seq_stride};
+    const uint32_t sbx[4] = {C::NB, 1, C::TP, 1};
+    if (make_tmap_4d(&tks, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.kv.Ks, sd, ss, sbx, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return BG_EUNSUPPORTED;
+    if (make_tmap_4d(&tvs, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.kv.Vs, sd, ss, sbx, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return BG_EUNSUPPORTED;
+  } else {
+    tks = tk;
+    tvs = tv;
+  }
+  TcParams p;
+  p.q = a.q;
+  p.q_f16 = a.q_f16;
+  p.partials = a.partials;
+  p.B = a.B;
+  p.S = a.S;
+  p.H = a.H;
+  p.KV = a.KV;
+  p.G = a.H / a.KV;
+  p.M = a.S * p.G;
+  p.posBase = a.posBase;
+  p.pos_lo = a.pos_lo;
+  p.pos_hi = a.pos_hi;
+  p.chunk = a.chunk;
+  p.row_offset = a.kv.row_offset;
+  p.nrows_total = a.B * a.S * a.H;
+  p.sl2 = a.scale * kLog2e;
+  auto kern = attn_tc_kernel<MODE, D, NT>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
+    return BG_ELAUNCH;
+  kern<<<dim3(a.nsplit, a.B * a.KV), 160, C::SMEM, st>>>(tk, tv, tks, tvs, p);
+  return cudaGetLastError() == cudaSuccess ? BG_OK : BG_ELAUNCH;
+}
+
+template <int MODE, int D, int NT>
+int occupancy() {
+  using C = Cfg<MODE, D>;
+  static int cached = 0;
+  if (!cached) {
+    int n = 0;
+    auto kern = attn_tc_kernel<MODE, D, NT>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, 160, C::SMEM) != cudaSuccess || n < 1) n = 1;
+    cached = n;
+  }
+  return cached;
+}
+
+template <int MODE>
+int launch_mode(const AttnArgs &a, uint32_t M, cudaStream_t st) {
+  if (a.D == 128) return M <= 8 ? launch_cfg<MODE, 128, 1>(a, st) : launch_cfg<MODE, 128, 2>(a, st);
+  if (a.D == 256 && M <= 8) return launch_cfg<MODE, 256, 1>(a, st);
+  return BG_EUNSUPPORTED;
+}
+
+}  // namespace
+
+bool attn_tc_supported(int mode, uint32_t D, uint32_t S, uint32_t H, uint32_t KV, bool roll, bool ring) {
+  if (roll || ring) return false;  // rope-at-read / ring mapping: generic path
+  if (mode != BG_KV_F16 && mode != BG_KV_Q8) return false;
+  const uint32_t M = S * (H / KV);
+  if (D == 128) return M <= 16;
+  if (D == 256) return M <= 8;
+  return false;
+}
+
+int attn_tc_ctas_per_sm(int mode, uint32_t D, uint32_t M) {
+  if (mode == BG_KV_F16) {
+    if (D == 256) return occupancy<BG_KV_F16, 256, 1>();
+    return M <= 8 ? occupancy<BG_KV_F16, 128, 1>() : occupancy<BG_KV_F16, 128, 2>();
+  }
+  if (D == 256) return occupancy<BG_KV_Q8, 256, 1>();
+  return M <= 8 ? occupancy<BG_KV_Q8, 128, 1>() : occupancy<BG_KV_Q8, 128, 2>();
+}
+
+int launch_attn_tc(const AttnArgs &a, cudaStream_t st) {
+  if (!attn_tc_supported(a.mode, a.D, a.S, a.H, a.KV, a.cosT != nullptr, a.kv.window != 0)) return BG_EUNSUPPORTED;
+  const uint32_t M = a.S * (a.H / a.KV);
+  return a.mode == BG_KV_F16 ? launch_mode<BG_KV_F16>(a, M, st) : launch_mode<BG_KV_Q8>(a, M, st);
+}
+
+int poll_device_error_attn_tc() {
+  int v = 0, z = 0;
+  if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)) != cudaSuccess) return BG_ELAUNCH;
+  if (v) cudaMemcpyToSymbol(g_device_error, &z, sizeof(int));
+  return v;
+}
+
 }  // namespace bg

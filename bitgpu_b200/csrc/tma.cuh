@@ -13,7 +13,9 @@ namespace bg {
 
 constexpr uint32_t kSpinLimit = 1u << 24;
 
-extern __device__ int g_device_error;
+// Per-translation-unit timeout flag (no relocatable device code): each .cu that includes this
+// header exposes a host poll function that reads and clears its copy; bg_device_status polls all.
+static __device__ int g_device_error = 0;
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 

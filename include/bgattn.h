@@ -61,6 +61,15 @@ typedef struct {
 
 const char *bg_strerror(int code);
 int bg_version(void);
+/* Synchronise `stream`, then report (and clear) a bounded device wait that gave up in any kernel
+ * of this library since the last call: BG_ETIMEOUT, else BG_OK.  Every spin on an mbarrier in
+ * these kernels is bounded; on expiry the kernel records the timeout and returns instead of
+ * hanging (the engine's device-lost path, engine.ts:400-409, is the reference counterpart). */
+int bg_device_status(bg_stream_t stream);
+/* Route every attention call through the CUDA-core kernel instead of the tensor-core one (the
+ * reference's forceNoSubgroups option, src/types.ts / engine.ts:282, which forces the _wg
+ * fallback kernels).  Process-wide; returns the previous setting.  For A/B checks only. */
+int bg_force_generic(int on);
 
 /* ---- attention (decode S small, prefill / PLD verify S > 1) -------------------------------
  * Replaces the ATT dispatch of src/engine.ts:1543 (fused decode) and :1580 (prefill), i.e.

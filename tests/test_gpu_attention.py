@@ -165,3 +165,33 @@ def test_abi_errors(ops):
     cache = ops.KVCache(1, 16, 2, 128, mode="f16")
     with pytest.raises(BgError):
         ops.attention(q, cache, 16)         # posBase + S > capacity
+
+
+@pytest.mark.parametrize("mode", ["f16", "q8"])
+@pytest.mark.parametrize("shape", [(64, 1, 32, 8, 128, 32767), (3, 2, 32, 8, 128, 5000), (2, 4, 32, 8, 128, 700),
+                                   (1, 1, 24, 4, 256, 131071 // 4), (2, 1, 16, 8, 128, 2047), (1, 3, 6, 6, 128, 90)])
+def test_tensor_core_vs_generic(ops, mode, shape):
+    """The tensor-core decode kernel and the CUDA-core kernel agree (both also match the oracle
+    in the tests above); shapes cover G = 1..6, 1..16 rows per group and long contexts."""
+    from bitgpu_b200._lib import lib
+    B, S, H, KV, D, pb = shape
+    g = torch.Generator(device="cuda").manual_seed(sum(shape))
+    cache = ops.KVCache(B, pb + S, KV, D, mode=mode)
+    cache.append(0, torch.randn((B, pb + S, KV, D), generator=g, device="cuda"), 0)
+    cache.append(1, torch.randn((B, pb + S, KV, D), generator=g, device="cuda"), 0)
+    q = torch.randn((B, S, H, D), generator=g, device="cuda")
+    a = ops.attention(q, cache, pb)
+    prev = lib().bg_force_generic(1)
+    try:
+        b = ops.attention(q, cache, pb)
+    finally:
+        lib().bg_force_generic(prev)
+    err = (a - b).abs().max().item()
+    assert err < 1e-3, err
+    assert lib().bg_device_status(None) == 0
+
+
+def test_tc_oracle_spot(ops):
+    """Tensor-core path vs oracle at the config-2 shape (2 sequences sampled)."""
+    for mode in ("f16", "q8"):
+        run_case(ops, mode, B=2, S=1, H=32, KV=8, D=128, pos_base=32767, seed=31)
