@@ -48,6 +48,11 @@ def parse():
     ap.add_argument("--batch", type=int, default=B, help="sequences per GPU (profiling runs use fewer)")
     ap.add_argument("--modes", default="f16,q8", help="KV modes to run (the first is the headline)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
+                    help="decode: config 2 headline (+ prefill variant); prefill: config 3 alone")
+    ap.add_argument("--seq", type=int, default=8192, help="prefill tokens per sequence (config 3: 8192)")
+    ap.add_argument("--prefill-batch", type=int, default=8, help="prefill sequences per GPU (config 3: 8)")
+    ap.add_argument("--no-prefill", action="store_true")
     return ap.parse_args()
 
 
@@ -236,6 +241,51 @@ def profiled_traffic(mode, batch):
     return None
 
 
+# config 3; manifest models/bonsai-4b-gguf: heads 32, kv_heads 8, head_dim 128
+PF_H, PF_KV = 32, 8
+
+
+def prefill_flops(batch, seq):
+    """QK^T and PV over the causal half including the diagonal, 2 flop per MAC."""
+    return 4.0 * D * PF_H * batch * seq * (seq + 1) / 2
+
+
+def run_prefill(torch, ops, args, rank, barrier, max_over_ranks, clocks_for=None):
+    """Config 3: causal prefill attention of `batch` x `seq` f16 tokens over the f16 cache those
+    tokens were appended to (posBase 0), f16 output; then the step's K/V rows written into an f16
+    and a q8 cache (timed separately, as bytes)."""
+    nb, S = args.prefill_batch, args.seq
+    g = torch.Generator(device="cuda").manual_seed(7 + rank)
+    k16 = torch.randn((nb, S, PF_KV, D), generator=g, device="cuda").half()
+    v16 = torch.randn((nb, S, PF_KV, D), generator=g, device="cuda").half()
+    cache = ops.KVCache(nb, S, PF_KV, D, mode="f16", device="cuda")
+    cache.append(0, k16, 0)
+    cache.append(1, v16, 0)
+    q = torch.randn((nb, S, PF_H, D), generator=g, device="cuda").half()
+    out = torch.empty((nb, S, PF_H, D), device="cuda", dtype=torch.float16)
+    clk = Clocks(clocks_for) if clocks_for is not None else None
+    ms = max_over_ranks(time_steps(torch, lambda: ops.attention(q, cache, 0, out=out), args.steps, args.warmup,
+                                   barrier))
+    res = {"ms": ms, "flops": prefill_flops(nb, S)}
+    if clk:
+        res["clocks"] = clk.stop()
+    # the prefill's K/V written into an f16 cache and a q8 cache (kv append, HBM-bound)
+    c16 = ops.KVCache(nb, S, PF_KV, D, mode="f16", device="cuda")
+    c8 = ops.KVCache(nb, S, PF_KV, D, mode="q8", device="cuda")
+
+    def writes():
+        for c in (c16, c8):
+            c.append(0, k16, 0)
+            c.append(1, v16, 0)
+    wms = max_over_ranks(time_steps(torch, writes, max(3, args.steps // 4), 2, barrier))
+    wbytes = 2 * k16.numel() * 2 * 2 + 2 * k16.numel() * (2 + 1) + 2 * (k16.numel() // 32) * 4
+    res["kv_write"] = {"ms": round(wms, 4), "GB/s": round(wbytes / (wms * 1e-3) / 1e9, 1),
+                       "bytes": wbytes, "note": "K and V of the prefill into an f16 and a q8 cache"}
+    del cache, c16, c8, q, out
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_ours(args):
     import torch
     ws, rank, local = dist_env()
@@ -257,6 +307,27 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    _, bf16_peak, _ = peaks()
+    if args.workload == "prefill":
+        r = run_prefill(torch, ops, args, rank, barrier, max_over_ranks, clocks_for=local)
+        if rank == 0:
+            tf = r["flops"] * ws / (r["ms"] * 1e-3) / 1e12
+            per = r["flops"] / (r["ms"] * 1e-3) / 1e12
+            print(json.dumps({
+                "metric": "prefill-attn TFLOP/s (config 3, Qwen3-4B shape, causal, f16)", "value": round(tf, 2),
+                "unit": "TFLOP/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(r["ms"], 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f16", "data": "synthetic N(0,1), seeded",
+                "config": {"workload": f"config 3: causal prefill, H32 KV8 D128, batch {args.prefill_batch}, "
+                                       f"seq {args.seq}, f16 Q/K/V, f32 accumulate, f16 out",
+                           "l2": "Q+K/V+out >> 126 MB L2"},
+                "roofline": {"bound": "tensor", "achieved": round(per, 1), "peak": bf16_peak, "unit": "TFLOP/s",
+                             "frac": round(per / bf16_peak, 4), "peak_kind": "measured cuBLAS bf16 burst",
+                             "traffic": None},
+                "gpu_launches": args.steps, "clocks": r.get("clocks"), "kv_write": r["kv_write"]}), flush=True)
+        if dist:
+            dist.destroy_process_group()
+        return
     q = torch.randn((nb, 1, H, D), device="cuda", generator=torch.Generator(device="cuda").manual_seed(100 + rank))
     results = {}
     for i, mode in enumerate(modes):
@@ -298,6 +369,11 @@ def run_ours(args):
         results[mode] = res
         del cache
         torch.cuda.empty_cache()
+    pf = None
+    if not args.no_prefill:
+        pa = argparse.Namespace(**vars(args))
+        pa.steps, pa.warmup = max(3, min(args.steps, 20)), 3
+        pf = run_prefill(torch, ops, pa, rank, barrier, max_over_ranks)
 
     if rank != 0:
         if dist:
@@ -324,6 +400,13 @@ def run_ours(args):
                          "frac": round(r["per_gpu_gbs"] / hbm, 4), "bytes_per_step_per_gpu": r["bytes"]}
                      for m, r in results.items() if m != modes[0]},
     }
+    if pf:
+        tf = pf["flops"] / (pf["ms"] * 1e-3) / 1e12
+        line["variants"]["prefill"] = {
+            "metric": "prefill-attn TFLOP/s (config 3)", "value": round(tf * ws, 2), "unit": "TFLOP/s",
+            "ms_per_step": round(pf["ms"], 4), "frac": round(tf / bf16_peak, 4),
+            "peak": bf16_peak, "peak_kind": "measured cuBLAS bf16 burst", "flops_per_step_per_gpu": pf["flops"],
+            "kv_write": pf["kv_write"]}
     if "e2e" in head:
         line["e2e"] = head["e2e"]
     if ws == 1 and not args.no_cpu_baseline:

@@ -5,6 +5,7 @@
 
 #include "attn.h"
 #include "kv.h"
+#include "prefill.h"
 
 using namespace bg;
 
@@ -56,6 +57,26 @@ int run_attention(const bg_attn_params *p, uint32_t batch, const void *q, uint32
                   const float *cosT, const float *sinT, float scale, uint32_t pos_lo, uint32_t pos_hi,
                   uint32_t row_offset, float *partials_out, const float *gate, void *out, uint32_t out_dtype,
                   void *ws, size_t ws_bytes, cudaStream_t st) {
+  const float sc = scale > 0.f ? scale : 1.0f / sqrtf((float)p->D);
+  // dense prefill on the tensor cores (f16 queries over an f16 cache, whole causal range)
+  if (!partials_out && !gate && !g_force_generic &&
+      prefill_tc_supported((int)kv->mode, p->D, p->S, q_dtype == BG_DT_F16, cosT != nullptr, kv->window != 0)) {
+    PrefillArgs pa;
+    pa.q = q;
+    pa.K = kv->K;
+    pa.V = kv->V;
+    pa.seq_stride = kv->seq_stride;
+    pa.out = out;
+    pa.out_f16 = out_dtype == BG_DT_F16;
+    pa.B = batch;
+    pa.S = p->S;
+    pa.H = p->H;
+    pa.KV = p->KV;
+    pa.posBase = p->posBase;
+    pa.Ltot = p->Ltot;
+    pa.scale = sc;
+    return launch_prefill_tc(pa, st);
+  }
   AttnArgs a;
   a.q = q;
   a.q_f16 = q_dtype == BG_DT_F16;
@@ -63,7 +84,7 @@ int run_attention(const bg_attn_params *p, uint32_t batch, const void *q, uint32
   a.mode = (int)kv->mode;
   a.cosT = cosT;
   a.sinT = sinT;
-  a.scale = scale > 0.f ? scale : 1.0f / sqrtf((float)p->D);
+  a.scale = sc;
   a.B = batch;
   a.S = p->S;
   a.H = p->H;
@@ -72,6 +93,9 @@ int run_attention(const bg_attn_params *p, uint32_t batch, const void *q, uint32
   a.posBase = p->posBase;
   a.pos_lo = pos_lo;
   a.pos_hi = pos_hi;
+  a.out = nullptr;
+  a.out_f16 = 0;
+  a.gate = nullptr;
   const uint64_t rows = (uint64_t)batch * p->S * p->H;
   const uint32_t L = pos_hi > pos_lo ? pos_hi - pos_lo : 1;
   const bool tc = !g_force_generic && attn_tc_supported(a.mode, p->D, p->S, p->H, p->KV, cosT != nullptr,
@@ -82,11 +106,23 @@ int run_attention(const bg_attn_params *p, uint32_t batch, const void *q, uint32
     if (n >= 1) a.nsplit = n < mx ? n : mx;
   }
   a.chunk = ((L + a.nsplit - 1) / a.nsplit + 63) / 64 * 64;  // whole 64-position tiles
-  if (ws_bytes < part_bytes(a.nsplit, rows, p->D) || (!ws && rows)) return BG_ENOMEM;
-  a.partials = static_cast<float *>(ws);
+  if (a.nsplit == 1) {
+    // one split: the kernel writes the final rows (or the caller's partial rows) itself
+    if (partials_out) {
+      a.partials = partials_out;
+    } else {
+      a.partials = nullptr;
+      a.out = out;
+      a.out_f16 = out_dtype == BG_DT_F16;
+      a.gate = gate;
+    }
+  } else {
+    if (ws_bytes < part_bytes(a.nsplit, rows, p->D) || (!ws && rows)) return BG_ENOMEM;
+    a.partials = static_cast<float *>(ws);
+  }
   int rc = tc ? launch_attn_tc(a, st) : BG_EUNSUPPORTED;
   if (rc == BG_EUNSUPPORTED) rc = launch_attn_generic(a, st);
-  if (rc) return rc;
+  if (rc || a.nsplit == 1) return rc;
   if (partials_out) return launch_lse_merge(a.partials, a.nsplit, (uint32_t)rows, p->D, nullptr, partials_out, -1, st);
   return launch_lse_merge(a.partials, a.nsplit, (uint32_t)rows, p->D, gate, out, out_dtype == BG_DT_F16, st);
 }
@@ -118,6 +154,7 @@ int bg_force_generic(int on) {
 int bg_device_status(bg_stream_t stream) {
   if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return BG_ELAUNCH;
   int e = poll_device_error_attn_tc();
+  if (!e) e = poll_device_error_prefill();
   return e ? (e < 0 ? e : BG_ELAUNCH) : BG_OK;
 }
 
@@ -125,7 +162,7 @@ size_t bg_attention_workspace_size(const bg_attn_params *p, uint32_t batch) {
   if (!p || !p->KV || !p->H) return 0;
   const uint32_t L = p->Ltot ? p->Ltot : 1;
   const uint32_t ns = attn_max_splits(batch, p->S, p->H, p->KV, p->D, L);
-  return part_bytes(ns, (uint64_t)batch * p->S * p->H, p->D);
+  return ns > 1 ? part_bytes(ns, (uint64_t)batch * p->S * p->H, p->D) : 0;  // one split needs no scratch
 }
 
 int bg_attention(const bg_attn_params *p, uint32_t batch, const void *q, uint32_t q_dtype, const bg_kv_cache *kv,

@@ -15,6 +15,11 @@ struct AttnArgs {
   uint32_t pos_lo, pos_hi;   // attended logical positions are clipped to [pos_lo, pos_hi)
   float *partials;           // [nsplit][B*S*H][D+2]: o[D], m (natural log units), l
   uint32_t nsplit, chunk;    // split j covers [pos_lo + j*chunk, pos_lo + (j+1)*chunk)
+  // direct mode (nsplit == 1 only): write the normalised (optionally gated) output instead of
+  // partials, so single-split calls need no workspace and no merge launch
+  void *out;
+  int out_f16;
+  const float *gate;
 };
 
 // Number of KV splits for one attention call over L positions with the given cache mode and

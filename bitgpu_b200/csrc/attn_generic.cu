@@ -162,6 +162,13 @@ __global__ void __launch_bounds__(128) attn_generic_kernel(AttnArgs a) {
     }
     const uint32_t qi = rr / G, h = kvh * G + rr % G;
     const uint64_t grow = ((uint64_t)b * a.S + qi) * a.H + h;
+    if (a.out) {  // single split: final output
+      float v = o / L;
+      if (a.gate) v = v / (1.0f + expf(-a.gate[grow * D + d]));
+      if (a.out_f16) static_cast<__half *>(a.out)[grow * D + d] = __float2half_rn(v);
+      else static_cast<float *>(a.out)[grow * D + d] = v;
+      continue;
+    }
     float *dst = a.partials + ((uint64_t)split * nrows_total + grow) * (D + 2);
     dst[d] = o;
     if (d == 0) {

@@ -34,6 +34,9 @@ struct TcParams {
   uint32_t posBase, pos_lo, pos_hi, chunk, row_offset;
   uint32_t nrows_total;
   float sl2;  // softmax scale * log2(e)
+  void *out;  // direct mode (single split)
+  int out_f16;
+  const float *gate;
 };
 
 template <int MODE, int D>
@@ -468,6 +471,13 @@ __global__ void __launch_bounds__(160, (MODE == BG_KV_Q8 && NT == 1 && D == 128)
     }
     const uint32_t qi = n / p.G, h = kvh * p.G + n % p.G;
     const uint64_t grow = ((uint64_t)b * p.S + qi) * p.H + h;
+    if (p.out) {  // single split: final output
+      float v = o / L;
+      if (p.gate) v = v / (1.0f + expf(-p.gate[grow * D + d]));
+      if (p.out_f16) static_cast<__half *>(p.out)[grow * D + d] = __float2half_rn(v);
+      else static_cast<float *>(p.out)[grow * D + d] = v;
+      continue;
+    }
     float *dst = p.partials + ((uint64_t)split * p.nrows_total + grow) * (D + 2);
     dst[d] = o;
     if (d == 0) {
@@ -519,6 +529,9 @@ int launch_cfg(const AttnArgs &a, cudaStream_t st) {
   p.row_offset = a.kv.row_offset;
   p.nrows_total = a.B * a.S * a.H;
   p.sl2 = a.scale * kLog2e;
+  p.out = a.out;
+  p.out_f16 = a.out_f16;
+  p.gate = a.gate;
   auto kern = attn_tc_kernel<MODE, D, NT>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
     return BG_ELAUNCH;
