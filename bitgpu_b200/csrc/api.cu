@@ -51,6 +51,14 @@ KVView make_view(const bg_kv_cache *kv, uint32_t KV, uint32_t row_offset) {
   return v;
 }
 
+// BGATTN_NSPLIT: split-count override for tuning sweeps (0 / unset = the cost model's choice).
+// bg_attention_workspace_size reserves for it, so an overridden call never under-allocates.
+uint32_t env_nsplit() {
+  const char *ov = getenv("BGATTN_NSPLIT");
+  const int n = ov ? atoi(ov) : 0;
+  return n > 0 ? (n < 512 ? (uint32_t)n : 512u) : 0u;
+}
+
 size_t part_bytes(uint32_t nsplit, uint64_t rows, uint32_t D) { return (size_t)nsplit * rows * (D + 2) * sizeof(float); }
 
 int run_attention(const bg_attn_params *p, uint32_t batch, const void *q, uint32_t q_dtype, const bg_kv_cache *kv,
@@ -101,10 +109,7 @@ int run_attention(const bg_attn_params *p, uint32_t batch, const void *q, uint32
   const bool tc = !g_force_generic && attn_tc_supported(a.mode, p->D, p->S, p->H, p->KV, cosT != nullptr,
                                                         kv->window != 0);
   a.nsplit = attn_num_splits(batch, p->S, p->H, p->KV, p->D, L, a.mode, tc);
-  if (const char *ov = getenv("BGATTN_NSPLIT")) {  // tuning sweeps only; bounded by the workspace sizing
-    const uint32_t n = (uint32_t)atoi(ov), mx = attn_max_splits(batch, p->S, p->H, p->KV, p->D, L);
-    if (n >= 1) a.nsplit = n < mx ? n : mx;
-  }
+  if (const uint32_t ov = env_nsplit()) a.nsplit = ov;
   a.chunk = ((L + a.nsplit - 1) / a.nsplit + 63) / 64 * 64;  // whole 64-position tiles
   if (a.nsplit == 1) {
     // one split: the kernel writes the final rows (or the caller's partial rows) itself
@@ -161,7 +166,8 @@ int bg_device_status(bg_stream_t stream) {
 size_t bg_attention_workspace_size(const bg_attn_params *p, uint32_t batch) {
   if (!p || !p->KV || !p->H) return 0;
   const uint32_t L = p->Ltot ? p->Ltot : 1;
-  const uint32_t ns = attn_max_splits(batch, p->S, p->H, p->KV, p->D, L);
+  uint32_t ns = attn_max_splits(batch, p->S, p->H, p->KV, p->D, L);
+  if (env_nsplit() > ns) ns = env_nsplit();
   return ns > 1 ? part_bytes(ns, (uint64_t)batch * p->S * p->H, p->D) : 0;  // one split needs no scratch
 }
 

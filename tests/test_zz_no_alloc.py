@@ -53,12 +53,15 @@ def test_noalloc_matches_workspace_entry_point_twice():
     _call_pair(L, ops, "q8", B=1, S=3, H=24, KV=4, D=256, pos_base=2000, seed=2, gated=True)
 
 
-def test_noalloc_rejects_oversized_scratch():
+def test_noalloc_rejects_oversized_scratch(monkeypatch):
+    """A call whose split partials would exceed the fixed 8 MiB is refused (BG_ENOMEM) before any
+    launch.  The split-count override forces 64 splits of 2048 rows (68 MB of partials)."""
     from bitgpu_b200 import ops
     from bitgpu_b200._lib import AttnParams, BG_ENOMEM, DT_F32, lib
     L = lib()
-    B, S, H, KV, D = 64, 64, 32, 8, 128     # partials far beyond 8 MiB
-    p = AttnParams(S, H, KV, D, 4096 - S, 4096)
+    monkeypatch.setenv("BGATTN_NSPLIT", "64")
+    B, S, H, KV, D = 64, 1, 32, 8, 128
+    p = AttnParams(S, H, KV, D, 32767, 32768)
     assert L.bg_attention_workspace_size(C.byref(p), B) > 8 << 20
     cache = ops.KVCache(1, 8, KV, D, mode="f16")
     d = cache.desc()
