@@ -28,6 +28,7 @@ sys.path.insert(0, ROOT)
 
 # config 2; manifest models/bonsai-8b-gguf: heads 32, kv_heads 8, head_dim 128
 B, L, H, KV, D = 64, 32768, 32, 8, 128
+GA_L_DEFAULT = 131072
 ROW_BYTES = {"f16": D * 2, "q8": D + (D // 32) * 4, "q8r": D + 4, "f32": D * 4}
 
 
@@ -48,11 +49,17 @@ def parse():
     ap.add_argument("--batch", type=int, default=B, help="sequences per GPU (profiling runs use fewer)")
     ap.add_argument("--modes", default="f16,q8", help="KV modes to run (the first is the headline)")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
-                    help="decode: config 2 headline (+ prefill variant); prefill: config 3 alone")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "gated", "deltanet", "roll"],
+                    help="decode: config 2 headline (+ the other configs as variants); others: one config alone")
+    ap.add_argument("--gated-ctx", type=int, default=GA_L_DEFAULT)
+    ap.add_argument("--dn-prefill", type=int, default=4096)
+    ap.add_argument("--roll-batch", type=int, default=32)
+    ap.add_argument("--roll-steps", type=int, default=2048)
+    ap.add_argument("--variants", default="q8,prefill,gated,deltanet,roll",
+                    help="configs measured as variants of the default decode run")
     ap.add_argument("--seq", type=int, default=8192, help="prefill tokens per sequence (config 3: 8192)")
     ap.add_argument("--prefill-batch", type=int, default=8, help="prefill sequences per GPU (config 3: 8)")
-    ap.add_argument("--no-prefill", action="store_true")
+
     return ap.parse_args()
 
 
@@ -286,6 +293,144 @@ def run_prefill(torch, ops, args, rank, barrier, max_over_ranks, clocks_for=None
     return res
 
 
+# config 5b; manifest models/bonsai-27b-gguf: heads 24, kv_heads 4, head_dim 256
+GA_H, GA_KV, GA_D, GA_L = 24, 4, 256, 131072
+
+
+def run_gated(torch, ops, args, ws, rank, barrier, max_over_ranks):
+    """Config 5b: one stream's gated head_dim-256 decode at 131072 positions, the cache split over
+    the ranks (bitgpu_b200.splitkv: partials + NCCL all-gather + LSE merge with the gate fused)."""
+    from bitgpu_b200.splitkv import SplitKVDecoder
+    L = args.gated_ctx
+    dec = SplitKVDecoder(L)
+    n = dec.hi - dec.lo
+    g = torch.Generator(device="cuda").manual_seed(11 + rank)
+    cache = ops.KVCache(1, n, GA_KV, GA_D, mode="f16", device="cuda")
+    for p0 in range(0, n, 8192):
+        m = min(8192, n - p0)
+        for w in (0, 1):
+            cache.append(w, torch.randn((1, m, GA_KV, GA_D), generator=g, device="cuda"), p0)
+    gq = torch.Generator(device="cuda").manual_seed(12)          # identical q / gate on every rank
+    q = torch.randn((1, 1, GA_H, GA_D), generator=gq, device="cuda")
+    gate = torch.randn((1, 1, GA_H, GA_D), generator=gq, device="cuda")
+    scale = 1.0 / GA_D ** 0.5
+    if ws == 1:
+        out = torch.empty_like(q)
+        fn = lambda: ops.attention(q, cache, L - 1, scale=scale, gate=gate, out=out)
+        launches = 1
+    else:
+        fn = lambda: dec.step(q, cache, L - 1, gate=gate, scale=scale)
+        launches = 2
+    ms = max_over_ranks(time_steps(torch, fn, args.steps, args.warmup, barrier))
+    byts = 2 * L * GA_KV * GA_D * 2 + 3 * GA_H * GA_D * 4
+    del cache
+    torch.cuda.empty_cache()
+    return {"ms": ms, "bytes": byts, "gbs": byts / (ms * 1e-3) / 1e9, "launches_per_step": launches,
+            "nccl_bytes_per_rank": 0 if ws == 1 else GA_H * (GA_D + 2) * 4}
+
+
+# config 5a (BASELINE.json configs[4]); 27B hybrid linear layer: 16 key heads, 48 value heads, 128 x 128
+DN_HK, DN_H, DN_DK, DN_DV = 16, 48, 128, 128
+
+
+def deltanet_decode_bytes():
+    """Per decode token: the f32 state in and out, q/k of the key heads, v/z/output of the value
+    heads, a/b gate inputs."""
+    return 2 * DN_H * DN_DK * DN_DV * 4 + (2 * DN_HK * DN_DK + 3 * DN_H * DN_DV + 2 * DN_H) * 4
+
+
+def run_deltanet(torch, ops, args, rank, barrier, max_over_ranks):
+    """Config 5a: a 4096-token gated-DeltaNet prefill (g/beta -> recurrence -> gated norm, one
+    fused launch) and then single-token decode steps continuing its state.  B=1 is one sequential
+    scan: multi-GPU runs are independent replicas."""
+    S = args.dn_prefill
+    g = torch.Generator(device="cuda").manual_seed(21 + rank)
+    r = lambda *sh: torch.randn(sh, generator=g, device="cuda")
+    q, k, v, z = r(S, DN_HK, DN_DK), r(S, DN_HK, DN_DK), r(S, DN_H, DN_DV), r(S, DN_H, DN_DV)
+    a, b = r(S, DN_H), r(S, DN_H)
+    a_neg, dt = -torch.ones(DN_H, device="cuda"), torch.zeros(DN_H, device="cuda")
+    gamma = torch.ones(DN_DV, device="cuda")
+    st = torch.zeros((DN_H, DN_DK, DN_DV), device="cuda")
+    pf = lambda: ops.deltanet_fused(q, k, v, a, b, a_neg, dt, z, gamma, 1e-6, state_in=None, state_out=st)
+    ms_pf = max_over_ranks(time_steps(torch, pf, max(2, args.steps // 10), 2, barrier))
+    q1, k1, v1, z1, a1, b1 = q[:1], k[:1], v[:1], z[:1], a[:1], b[:1]
+    dec = lambda: ops.deltanet_fused(q1, k1, v1, a1, b1, a_neg, dt, z1, gamma, 1e-6, state_in=st, state_out=st)
+    ms_dec = max_over_ranks(time_steps(torch, dec, args.steps, args.warmup, barrier))
+    flops_pf = S * DN_H * 4 * DN_DK * DN_DV * 2
+    return {"prefill_ms": ms_pf, "prefill_tokens": S, "prefill_tflops": flops_pf / (ms_pf * 1e-3) / 1e12,
+            "decode_ms": ms_dec, "decode_bytes": deltanet_decode_bytes(),
+            "decode_gbs": deltanet_decode_bytes() / (ms_dec * 1e-3) / 1e9}
+
+
+# config 4 (BASELINE.json configs[3]); Qwen3-1.7B shape: 16 Q / 8 KV heads, head_dim 128
+RL_H, RL_KV, RL_SINKS, RL_WINDOW = 16, 8, 4, 4096
+
+
+def rope_tables(torch, positions, D, theta=1e6, factor=4.0, orig=8192):
+    """YaRN rope tables [positions, D/2] in float64 angles, one float32 rounding (the reference's
+    synthRope recipe; manifest bonsai-1.7b-gguf: theta 1e6, yarn factor 4, orig 8192)."""
+    import math
+    half = D // 2
+    j = torch.arange(half, dtype=torch.float64)
+    pf = theta ** (2 * j / D)
+    lo = max(0, math.floor(D * math.log(orig / (32 * 2 * math.pi)) / (2 * math.log(theta))))
+    hi = min(half - 1, math.ceil(D * math.log(orig / (2 * math.pi)) / (2 * math.log(theta))))
+    ramp = ((j - lo) / (hi - lo)).clamp(0, 1)
+    inv = (1 / (factor * pf)) * ramp + (1 / pf) * (1 - ramp)
+    ms = float(torch.tensor(0.1 * math.log(factor) + 1, dtype=torch.float32))
+    ang = torch.outer(torch.arange(positions, dtype=torch.float64), inv)
+    return (torch.cos(ang) * ms).float().cuda(), (torch.sin(ang) * ms).float().cuda()
+
+
+def run_roll(torch, ops, args, rank, barrier, max_over_ranks):
+    """Config 4: sink-mode decode stream, batch 32, q8 ring of 4 sinks + 4096 slots.  Every step:
+    evictFor (ring head advance when full), append the step's unroped K and V, attention with
+    rope-at-read by logical slot.  Timed over `roll_steps` consecutive steps that cross
+    evictions; the metric is mean algorithmic GB/s over those steps."""
+    nb, maxlen = args.roll_batch, RL_SINKS + RL_WINDOW
+    cache = ops.KVCache(nb, maxlen, RL_KV, D, mode="q8", sinks=RL_SINKS, window=RL_WINDOW, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(31 + rank)
+    fill = maxlen - 1024                      # steady-state fill right after an eviction (3076)
+    for p0 in range(0, fill, 1024):
+        m = min(1024, fill - p0)
+        for w in (0, 1):
+            cache.append(w, torch.randn((nb, m, RL_KV, D), generator=g, device="cuda"), p0)
+    cos_t, sin_t = rope_tables(torch, maxlen, D)
+    T = args.roll_steps
+    ks = torch.randn((T, nb, 1, RL_KV, D), generator=g, device="cuda")
+    vs = torch.randn((T, nb, 1, RL_KV, D), generator=g, device="cuda")
+    qs = torch.randn((T, nb, 1, RL_H, D), generator=g, device="cuda")
+    out = torch.empty((nb, 1, RL_H, D), device="cuda")
+    state = {"fill": fill, "t": 0, "bytes": 0}
+
+    def step():
+        t = state["t"] % T
+        f = cache.evict_for(state["fill"], 1, maxlen)
+        cache.append(0, ks[t], f)
+        cache.append(1, vs[t], f)
+        ops.attention(qs[t], cache, f, cos_t=cos_t, sin_t=sin_t, out=out)
+        state["fill"] = f + 1
+        state["t"] += 1
+        state["bytes"] += nb * 2 * (f + 1) * RL_KV * (D + 16) + (f + 1) * (D // 2) * 8
+    for _ in range(3):
+        step()
+    state["bytes"] = 0
+    ms = time_steps(torch, step, T, 0, barrier)
+    byts = state["bytes"] / T
+    ms = max_over_ranks(ms)
+    del cache
+    torch.cuda.empty_cache()
+    return {"ms": ms, "bytes_per_step": byts, "gbs": byts / (ms * 1e-3) / 1e9, "steps": T,
+            "fill_range": [maxlen - 1024, maxlen], "ring_head": None}
+
+
+def _base_line(args, ws, metric, value, unit, ms, dtype, config, roofline, launches, clocks=None):
+    return {"metric": metric, "value": round(value, 3), "unit": unit, "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": dtype, "data": "synthetic N(0,1), seeded", "config": config,
+            "roofline": roofline, "gpu_launches": launches, "clocks": clocks}
+
+
 def run_ours(args):
     import torch
     ws, rank, local = dist_env()
@@ -296,9 +441,8 @@ def run_ours(args):
         dist.init_process_group("nccl")
     barrier = (lambda: dist.barrier()) if dist else (lambda: None)
     from bitgpu_b200 import ops
-    hbm, _, peak_kind = peaks()
+    hbm, bf16_peak, peak_kind = peaks()
     nb = args.batch
-    modes = [m for m in args.modes.split(",") if m]
 
     def max_over_ranks(ms):
         if not dist:
@@ -307,27 +451,75 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    _, bf16_peak, _ = peaks()
-    if args.workload == "prefill":
-        r = run_prefill(torch, ops, args, rank, barrier, max_over_ranks, clocks_for=local)
+    def finish(line):
         if rank == 0:
-            tf = r["flops"] * ws / (r["ms"] * 1e-3) / 1e12
-            per = r["flops"] / (r["ms"] * 1e-3) / 1e12
-            print(json.dumps({
-                "metric": "prefill-attn TFLOP/s (config 3, Qwen3-4B shape, causal, f16)", "value": round(tf, 2),
-                "unit": "TFLOP/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
-                "ms_per_step": round(r["ms"], 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-                "dtype": "f16", "data": "synthetic N(0,1), seeded",
-                "config": {"workload": f"config 3: causal prefill, H32 KV8 D128, batch {args.prefill_batch}, "
-                                       f"seq {args.seq}, f16 Q/K/V, f32 accumulate, f16 out",
-                           "l2": "Q+K/V+out >> 126 MB L2"},
-                "roofline": {"bound": "tensor", "achieved": round(per, 1), "peak": bf16_peak, "unit": "TFLOP/s",
-                             "frac": round(per / bf16_peak, 4), "peak_kind": "measured cuBLAS bf16 burst",
-                             "traffic": None},
-                "gpu_launches": args.steps, "clocks": r.get("clocks"), "kv_write": r["kv_write"]}), flush=True)
+            print(json.dumps(line), flush=True)
         if dist:
             dist.destroy_process_group()
-        return
+
+    def hbm_roof(gbs_per_gpu, note, traffic=None):
+        return {"bound": "hbm", "achieved": round(gbs_per_gpu, 1), "peak": hbm, "unit": "GB/s",
+                "frac": round(gbs_per_gpu / hbm, 4), "peak_kind": f"{peak_kind} (copy, read+write)",
+                "traffic": traffic, "note": note}
+
+    # ---------------- single-config workloads ----------------
+    if args.workload == "prefill":
+        clk = Clocks(local)
+        r = run_prefill(torch, ops, args, rank, barrier, max_over_ranks)
+        per = r["flops"] / (r["ms"] * 1e-3) / 1e12
+        line = _base_line(args, ws, "prefill-attn TFLOP/s (config 3, Qwen3-4B shape, causal, f16)", per * ws,
+                          "TFLOP/s", r["ms"], "f16",
+                          {"workload": f"config 3: causal prefill, H32 KV8 D128, batch {args.prefill_batch}, "
+                                       f"seq {args.seq}, f16 Q/K/V, f32 accumulate, f16 out",
+                           "l2": "Q + K/V + out >> 126 MB L2"},
+                          {"bound": "tensor", "achieved": round(per, 1), "peak": bf16_peak, "unit": "TFLOP/s",
+                           "frac": round(per / bf16_peak, 4), "peak_kind": f"{peak_kind} cuBLAS bf16 burst",
+                           "traffic": None}, args.steps, clk.stop())
+        line["kv_write"] = r["kv_write"]
+        return finish(line)
+    if args.workload == "gated":
+        clk = Clocks(local)
+        r = run_gated(torch, ops, args, ws, rank, barrier, max_over_ranks)
+        line = _base_line(args, ws, "gated decode-attn HBM GB/s (config 5b, 27B hybrid, D256, f16, split-KV)",
+                          r["gbs"], "GB/s", r["ms"], "f16",
+                          {"workload": f"config 5b: one stream, H24 KV4 D256, ctx {args.gated_ctx} f16, sigmoid "
+                                       f"gate, KV positions split over {ws} GPU(s), NCCL all-gather + LSE merge",
+                           "l2": "cache 537 MB >> 126 MB L2", "scaling_note": "fixed total work (strong)"},
+                          hbm_roof(r["gbs"] / ws, "per-GPU share of the step's algorithmic bytes / step time"),
+                          r["launches_per_step"] * args.steps, clk.stop())
+        line["scaling"] = "strong"
+        line["nccl_bytes_per_rank_per_step"] = r["nccl_bytes_per_rank"]
+        return finish(line)
+    if args.workload == "deltanet":
+        clk = Clocks(local)
+        r = run_deltanet(torch, ops, args, rank, barrier, max_over_ranks)
+        line = _base_line(args, ws, "deltanet decode HBM GB/s (config 5a, 27B hybrid linear layer)",
+                          r["decode_gbs"] * ws, "GB/s", r["decode_ms"], "f32",
+                          {"workload": "config 5a: gated DeltaNet, HK16 H48 DK=DV=128, B=1 per GPU (replicas), "
+                                       f"{r['prefill_tokens']}-token fused prefill then decode"},
+                          hbm_roof(r["decode_gbs"], "state in+out + token inputs per decode launch"),
+                          args.steps, clk.stop())
+        line["prefill"] = {"ms": round(r["prefill_ms"], 3), "tokens": r["prefill_tokens"],
+                           "TFLOP/s": round(r["prefill_tflops"], 3), "form": "recurrent scan, fused g/beta + norm"}
+        return finish(line)
+    if args.workload == "roll":
+        clk = Clocks(local)
+        r = run_roll(torch, ops, args, rank, barrier, max_over_ranks)
+        line = _base_line(args, ws, "sink-window decode HBM GB/s (config 4, q8 ring, rope-at-read)",
+                          r["gbs"] * ws, "GB/s", r["ms"], "q8",
+                          {"workload": f"config 4: H16 KV8 D128, batch {args.roll_batch}, 4 sinks + 4096 ring, "
+                                       f"{r['steps']} consecutive decode steps from fill 3076 (crossing "
+                                       f"evictions)", "l2": "cache ~150 MB >> L2 only partly"},
+                          hbm_roof(r["gbs"], "mean algorithmic bytes per step / mean step time (append x2 + "
+                                             "attention)"), 3 * r["steps"], clk.stop())
+        line["steps"] = r["steps"]
+        return finish(line)
+
+    # ---------------- default: config-2 decode headline + variants ----------------
+    variants = [v for v in args.variants.split(",") if v]
+    modes = [m for m in args.modes.split(",") if m]
+    if "q8" in variants and "q8" not in modes:
+        modes.append("q8")
     q = torch.randn((nb, 1, H, D), device="cuda", generator=torch.Generator(device="cuda").manual_seed(100 + rank))
     results = {}
     for i, mode in enumerate(modes):
@@ -369,11 +561,37 @@ def run_ours(args):
         results[mode] = res
         del cache
         torch.cuda.empty_cache()
-    pf = None
-    if not args.no_prefill:
-        pa = argparse.Namespace(**vars(args))
-        pa.steps, pa.warmup = max(3, min(args.steps, 20)), 3
-        pf = run_prefill(torch, ops, pa, rank, barrier, max_over_ranks)
+
+    short = argparse.Namespace(**vars(args))
+    short.steps, short.warmup = max(3, min(args.steps, 20)), 3
+    extra = {}
+    if "prefill" in variants:
+        pf = run_prefill(torch, ops, short, rank, barrier, max_over_ranks)
+        tf = pf["flops"] / (pf["ms"] * 1e-3) / 1e12
+        extra["prefill"] = {"metric": "prefill-attn TFLOP/s (config 3)", "value": round(tf * ws, 2),
+                            "unit": "TFLOP/s", "ms_per_step": round(pf["ms"], 4), "frac": round(tf / bf16_peak, 4),
+                            "peak": bf16_peak, "peak_kind": f"{peak_kind} cuBLAS bf16 burst",
+                            "flops_per_step_per_gpu": pf["flops"], "kv_write": pf["kv_write"]}
+    if "gated" in variants:
+        gs = argparse.Namespace(**vars(short))
+        gs.steps = max(20, short.steps)
+        r = run_gated(torch, ops, gs, ws, rank, barrier, max_over_ranks)
+        extra["gated_d256"] = {"metric": "config 5b gated decode GB/s (split-KV over the GPUs)",
+                               "value": round(r["gbs"], 1), "unit": "GB/s", "ms_per_step": round(r["ms"], 4),
+                               "frac": round(r["gbs"] / ws / hbm, 4), "scaling": "strong"}
+    if "deltanet" in variants:
+        r = run_deltanet(torch, ops, short, rank, barrier, max_over_ranks)
+        extra["deltanet"] = {"metric": "config 5a DeltaNet decode GB/s (per GPU, replicas)",
+                             "value": round(r["decode_gbs"] * ws, 1), "unit": "GB/s",
+                             "decode_ms": round(r["decode_ms"], 4), "frac": round(r["decode_gbs"] / hbm, 4),
+                             "prefill_4096_ms": round(r["prefill_ms"], 3)}
+    if "roll" in variants:
+        rs = argparse.Namespace(**vars(short))
+        rs.roll_steps = min(args.roll_steps, 1100)
+        r = run_roll(torch, ops, rs, rank, barrier, max_over_ranks)
+        extra["roll_q8"] = {"metric": "config 4 sink-window decode GB/s", "value": round(r["gbs"] * ws, 1),
+                            "unit": "GB/s", "ms_per_step": round(r["ms"], 4), "frac": round(r["gbs"] / hbm, 4),
+                            "steps": r["steps"]}
 
     if rank != 0:
         if dist:
@@ -381,32 +599,19 @@ def run_ours(args):
         return
     head = results[modes[0]]
     per_launch = head["bytes"] / (head["ms"] * 1e-3) / 1e9
-    traffic = profiled_traffic(modes[0], nb)
-    line = {
-        "metric": METRIC, "value": round(head["gbs"], 2), "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(head["ms"], 4), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": modes[0],
-        "data": "synthetic N(0,1), seeded; KV written through the library's own f16/q8 append",
-        "config": dict(CONFIG, global_batch_per_gpu=nb, kv_mode=modes[0]),
-        "roofline": {"bound": "hbm", "achieved": round(per_launch, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(per_launch / hbm, 4), "peak_kind": f"{peak_kind} (copy, read+write)",
-                     "traffic": traffic, "algorithmic_bytes": head["bytes"],
-                     "note": "achieved = algorithmic bytes per launch (2*B*L*KV*rowB + 2*B*H*D*4) / mean duration "
-                             "of one bg_attention call (split-KV kernel + LSE merge), CUDA events on its stream; "
-                             "traffic = ncu dram read+write bytes per sequence (profiles/) x batch"},
-        "gpu_launches": 2 * args.steps,
-        "clocks": head["clocks"],
-        "variants": {m: {"value": round(r["gbs"], 2), "unit": "GB/s", "ms_per_step": round(r["ms"], 4),
-                         "frac": round(r["per_gpu_gbs"] / hbm, 4), "bytes_per_step_per_gpu": r["bytes"]}
-                     for m, r in results.items() if m != modes[0]},
-    }
-    if pf:
-        tf = pf["flops"] / (pf["ms"] * 1e-3) / 1e12
-        line["variants"]["prefill"] = {
-            "metric": "prefill-attn TFLOP/s (config 3)", "value": round(tf * ws, 2), "unit": "TFLOP/s",
-            "ms_per_step": round(pf["ms"], 4), "frac": round(tf / bf16_peak, 4),
-            "peak": bf16_peak, "peak_kind": "measured cuBLAS bf16 burst", "flops_per_step_per_gpu": pf["flops"],
-            "kv_write": pf["kv_write"]}
+    line = _base_line(args, ws, METRIC, head["gbs"], "GB/s", head["ms"], modes[0],
+                      dict(CONFIG, global_batch_per_gpu=nb, kv_mode=modes[0]),
+                      hbm_roof(per_launch, "achieved = algorithmic bytes per launch (2*B*L*KV*rowB + 2*B*H*D*4) / "
+                                           "mean duration of one bg_attention call, CUDA events on its stream; "
+                                           "traffic = ncu dram read+write bytes per sequence (profiles/) x batch",
+                               traffic=profiled_traffic(modes[0], nb)),
+                      2 * args.steps, head["clocks"])
+    line["roofline"]["algorithmic_bytes"] = head["bytes"]
+    line["data"] = "synthetic N(0,1), seeded; KV written through the library's own f16/q8 append"
+    line["variants"] = {m: {"value": round(r["gbs"], 2), "unit": "GB/s", "ms_per_step": round(r["ms"], 4),
+                            "frac": round(r["per_gpu_gbs"] / hbm, 4), "bytes_per_step_per_gpu": r["bytes"]}
+                        for m, r in results.items() if m != modes[0]}
+    line["variants"].update(extra)
     if "e2e" in head:
         line["e2e"] = head["e2e"]
     if ws == 1 and not args.no_cpu_baseline:
