@@ -354,7 +354,10 @@ def run_deltanet(torch, ops, args, rank, barrier, max_over_ranks):
     pf = lambda: ops.deltanet_fused(q, k, v, a, b, a_neg, dt, z, gamma, 1e-6, state_in=None, state_out=st)
     ms_pf = max_over_ranks(time_steps(torch, pf, max(2, args.steps // 10), 2, barrier))
     q1, k1, v1, z1, a1, b1 = q[:1], k[:1], v[:1], z[:1], a[:1], b[:1]
-    dec = lambda: ops.deltanet_fused(q1, k1, v1, a1, b1, a_neg, dt, z1, gamma, 1e-6, state_in=st, state_out=st)
+    # one decode token, in place on the state, replayed as a captured CUDA graph (the per-token
+    # kernel is a few microseconds; host launch overhead would dominate otherwise)
+    dec = ops.Graphed(lambda: ops.deltanet_fused(q1, k1, v1, a1, b1, a_neg, dt, z1, gamma, 1e-6, state_in=st,
+                                                 state_out=st))
     ms_dec = max_over_ranks(time_steps(torch, dec, args.steps, args.warmup, barrier))
     flops_pf = S * DN_H * 4 * DN_DK * DN_DV * 2
     return {"prefill_ms": ms_pf, "prefill_tokens": S, "prefill_tflops": flops_pf / (ms_pf * 1e-3) / 1e12,

@@ -7,7 +7,7 @@ import ctypes as C
 import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libbgattn.so")
+LIB_PATH = os.environ.get("BGATTN_LIB") or os.path.join(HERE, "libbgattn.so")  # override: A/B builds
 
 BG_OK, BG_EINVAL, BG_ENOMEM, BG_ELAUNCH, BG_ETIMEOUT, BG_EUNSUPPORTED = 0, -1, -2, -3, -4, -5
 KV_F32, KV_F16, KV_Q8, KV_Q8R = 0, 1, 2, 3

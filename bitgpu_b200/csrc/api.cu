@@ -108,7 +108,7 @@ int run_attention(const bg_attn_params *p, uint32_t batch, const void *q, uint32
   const uint32_t L = pos_hi > pos_lo ? pos_hi - pos_lo : 1;
   const bool tc = !g_force_generic && attn_tc_supported(a.mode, p->D, p->S, p->H, p->KV, cosT != nullptr,
                                                         kv->window != 0);
-  a.nsplit = attn_num_splits(batch, p->S, p->H, p->KV, p->D, L, a.mode, tc);
+  a.nsplit = attn_num_splits(batch, p->S, p->H, p->KV, p->D, L, a.mode, tc, cosT != nullptr);
   if (const uint32_t ov = env_nsplit()) a.nsplit = ov;
   a.chunk = ((L + a.nsplit - 1) / a.nsplit + 63) / 64 * 64;  // whole 64-position tiles
   if (a.nsplit == 1) {

@@ -25,10 +25,11 @@ struct AttnArgs {
 // Number of KV splits for one attention call over L positions with the given cache mode and
 // kernel (tensor-core or not); the workspace holds nsplit * B*S*H * (D+2) floats.
 // attn_max_splits is the maximum over every mode/kernel (what workspace sizing reserves).
-uint32_t attn_num_splits(uint32_t B, uint32_t S, uint32_t H, uint32_t KV, uint32_t D, uint32_t L, int mode, bool tc);
+uint32_t attn_num_splits(uint32_t B, uint32_t S, uint32_t H, uint32_t KV, uint32_t D, uint32_t L, int mode, bool tc,
+                         bool roll = false);
 uint32_t attn_max_splits(uint32_t B, uint32_t S, uint32_t H, uint32_t KV, uint32_t D, uint32_t L);
 bool attn_tc_supported(int mode, uint32_t D, uint32_t S, uint32_t H, uint32_t KV, bool roll, bool ring);
-int attn_tc_ctas_per_sm(int mode, uint32_t D, uint32_t M);
+int attn_tc_ctas_per_sm(int mode, uint32_t D, uint32_t M, bool roll);
 int attn_generic_ctas_per_sm(int mode, uint32_t D, uint32_t rows, bool roll);
 
 int launch_attn_generic(const AttnArgs &a, cudaStream_t st);

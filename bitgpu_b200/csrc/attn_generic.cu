@@ -323,13 +323,14 @@ int attn_generic_ctas_per_sm(int mode, uint32_t D, uint32_t rows, bool roll) {
 // where a CTA's slice is the unit's cache bytes / n and `slots` = resident CTAs on 148 SMs.
 // The first term rewards filling the last wave; the second charges the split partials'
 // write + merge read.  Splits never get shorter than 256 positions.
-uint32_t attn_num_splits(uint32_t B, uint32_t S, uint32_t H, uint32_t KV, uint32_t D, uint32_t L, int mode, bool tc) {
+uint32_t attn_num_splits(uint32_t B, uint32_t S, uint32_t H, uint32_t KV, uint32_t D, uint32_t L, int mode, bool tc,
+                         bool roll) {
   const uint32_t G = H / KV;
   const uint32_t M = S * G;
   const uint32_t rb = D >= 256 ? 4 : 8;
   const uint64_t rowchunks = tc ? 1 : (M + rb - 1) / rb;
   const uint64_t units = (uint64_t)B * KV * rowchunks;
-  const int per_sm = tc ? attn_tc_ctas_per_sm(mode, D, M) : attn_generic_ctas_per_sm(mode, D, M, false);
+  const int per_sm = tc ? attn_tc_ctas_per_sm(mode, D, M, roll) : attn_generic_ctas_per_sm(mode, D, M, roll);
   const double slots = 148.0 * per_sm;
   const double unit_bytes = 2.0 * L * kv_row_bytes(mode, D);
   const double ramp = 2.0 * 64 * 2 * kv_row_bytes(mode, D);
@@ -356,9 +357,13 @@ uint32_t attn_max_splits(uint32_t B, uint32_t S, uint32_t H, uint32_t KV, uint32
     if (mode == BG_KV_Q8R && D % 128) continue;
     const uint32_t a = attn_num_splits(B, S, H, KV, D, L, mode, false);
     m = a > m ? a : m;
-    if (attn_tc_supported(mode, D, S, H, KV, false, false)) {
-      const uint32_t t = attn_num_splits(B, S, H, KV, D, L, mode, true);
-      m = t > m ? t : m;
+    for (int roll = 0; roll < 2; ++roll) {
+      if (attn_tc_supported(mode, D, S, H, KV, roll, false)) {
+        const uint32_t t = attn_num_splits(B, S, H, KV, D, L, mode, true, roll);
+        m = t > m ? t : m;
+      }
+      const uint32_t g = attn_num_splits(B, S, H, KV, D, L, mode, false, roll);
+      m = g > m ? g : m;
     }
   }
   return m;

@@ -5,7 +5,8 @@
 // path:
 //   * one producer warp streams K/V tiles of 64 positions for one (sequence, kv head) into shared
 //     memory with 4-D TMA tiled loads (128-byte swizzle, no multicast), through an NST-deep
-//     mbarrier ring;
+//     mbarrier ring (q8 block scales by cp.async; rope-at-read kernels use a ring-aware cp.async
+//     producer for everything);
 //   * four consumer warps each own 16 positions of a tile.  Scores are computed transposed,
 //     S^T = K . Q^T (m16n8k16: positions on M, the GQA group's query rows on N, head_dim on K),
 //     so the <= 8 query rows of a group pad only N to 8.  Q (f32) is split hi + lo into two f16
@@ -19,6 +20,7 @@
 // split partials [split][row][D+2] for the LSE merge kernel (shared with the generic path).
 #include <cuda.h>
 #include <cuda_fp16.h>
+#include <string.h>
 
 #include "attn.h"
 #include "tma.cuh"
@@ -37,6 +39,12 @@ struct TcParams {
   void *out;  // direct mode (single split)
   int out_f16;
   const float *gate;
+  // rope-at-read (sink mode): the cp.async producer's view of the cache and the rope tables
+  const float *cosT, *sinT;
+  const unsigned char *Kp, *Vp;
+  const float *Ksp, *Vsp;
+  uint64_t seq_stride;
+  uint32_t sinks, window, ring_head;
 };
 
 template <int MODE, int D>
@@ -88,14 +96,6 @@ __device__ __forceinline__ uint32_t pack_f16(float lo, float hi) {
   return *reinterpret_cast<uint32_t *>(&h);
 }
 
-// Two int8 codes of `w` (bytes picked by `sel`, see __byte_perm) -> exact f16x2.
-// 0x64XX as f16 is 1024 + XX; the codes are biased by 128 first, so subtract 1152.
-__device__ __forceinline__ uint32_t i8pair_f16(uint32_t w, uint32_t sel) {
-  const uint32_t r = __byte_perm(w ^ 0x80808080u, 0x64646464u, sel);
-  __half2 h = *reinterpret_cast<const __half2 *>(&r);
-  h = __hsub2(h, __half2(__float2half_rn(1152.f), __float2half_rn(1152.f)));
-  return *reinterpret_cast<uint32_t *>(&h);
-}
 constexpr uint32_t kSelLo = 0x4140, kSelHi = 0x4342, kSelEven = 0x4240, kSelOdd = 0x4341;
 
 // Biased form without the subtraction: (code + 1152) as exact f16x2, from a word already xored
@@ -116,8 +116,9 @@ __device__ __forceinline__ uint32_t swz(uint32_t base, int row, int gc) {
   return base + (gc >> 3) * (TP * 128) + row * 128 + (((gc & 7) ^ (row & 7)) << 4);
 }
 
-template <int MODE, int D, int NT>
-__global__ void __launch_bounds__(160, (MODE == BG_KV_Q8 && NT == 1 && D == 128) ? 3 : 1) attn_tc_kernel(const __grid_constant__ CUtensorMap tmK,
+template <int MODE, int D, int NT, bool ROLL>
+__global__ void __launch_bounds__(160, (MODE == BG_KV_Q8 && NT == 1 && D == 128 && !ROLL) ? 3 : 1) attn_tc_kernel(
+                                                      const __grid_constant__ CUtensorMap tmK,
                                                       const __grid_constant__ CUtensorMap tmV,
                                                       const __grid_constant__ CUtensorMap tmKs,
                                                       const __grid_constant__ CUtensorMap tmVs, TcParams p) {
@@ -139,41 +140,106 @@ __global__ void __launch_bounds__(160, (MODE == BG_KV_Q8 && NT == 1 && D == 128)
 
   if (tid == 0) {
     for (int s = 0; s < NST; ++s) {
-      mbar_init(&full[s], 1);
+      // ROLL: one cp.async arrival per producer lane; q8: lane 0's expect_tx + 32 cp.async arrivals
+      mbar_init(&full[s], ROLL ? 32 : (MODE == BG_KV_Q8 ? 33 : 1));
       mbar_init(&empty[s], C::NCW);
     }
     fence_barrier_init();
   }
   __syncthreads();
 
+  if (warp == C::NCW && ROLL) {  // ---------------- producer warp (cp.async, ring-aware) ----------------
+    // Logical slot -> physical row (sink slots, then the ring); every lane copies 16-byte chunks
+    // into the same 128B-swizzled layout TMA would produce; rows past `hi` are zero-filled.
+    constexpr int CPR = C::ROWB / 16;  // 16-byte chunks per cache row
+    bool ok = true;
+    for (int t = 0; t < ntiles && ok; ++t) {
+      const int s = t % NST;
+      if (t >= NST) ok = mbar_wait_warp(&empty[s], ((t / NST) - 1) & 1);
+      if (!ok) break;
+      const uint32_t st = smem_u32(smem + s * C::STAGE);
+      const uint32_t p0 = lo + t * TP;
+      for (int idx = lane; idx < TP * CPR; idx += 32) {
+        const int r = idx / CPR, gc = idx % CPR;
+        const uint32_t pl = p0 + r;
+        const bool valid = pl < hi;
+        uint32_t ph = pl - p.row_offset;
+        if (p.window && pl >= p.sinks) ph = p.sinks + (p.ring_head + (pl - p.sinks)) % p.window;
+        const uint64_t row = valid ? (((uint64_t)b * p.seq_stride + ph) * p.KV + kvh) : 0;
+        const unsigned char *srcK = p.Kp + row * C::ROWB + gc * 16;
+        const unsigned char *srcV = p.Vp + row * C::ROWB + gc * 16;
+        const uint32_t n = valid ? 16u : 0u;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(swz<TP>(st, r, gc)), "l"(srcK), "r"(n)
+                     : "memory");
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(swz<TP>(st + C::KVT, r, gc)), "l"(srcV),
+                     "r"(n)
+                     : "memory");
+        if constexpr (MODE == BG_KV_Q8) {
+          if (gc < NB / 4) {  // the row's block scales: NB floats = NB/4 chunks
+            const float *sk = p.Ksp + row * NB + gc * 4, *sv = p.Vsp + row * NB + gc * 4;
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(st + 2 * C::KVT + (r * NB + gc * 4) * 4),
+                         "l"(sk), "r"(n)
+                         : "memory");
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(st + 2 * C::KVT + C::SCT +
+                                                                              (r * NB + gc * 4) * 4),
+                         "l"(sv), "r"(n)
+                         : "memory");
+          }
+        }
+      }
+      asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&full[s])) : "memory");
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    return;
+  }
+
   if (warp == C::NCW) {  // ---------------- producer warp ----------------
-    if (lane == 0 && ntiles > 0) {
-      prefetch_tmap(&tmK);
-      prefetch_tmap(&tmV);
-      if constexpr (MODE == BG_KV_Q8) {
-        prefetch_tmap(&tmKs);
-        prefetch_tmap(&tmVs);
+    // Lane 0 streams the K/V rows with TMA (expect_tx of exactly those bytes).  q8 block scales
+    // (16-byte rows) are fetched by all 32 lanes with cp.async and signalled through
+    // cp.async.mbarrier.arrive.noinc, so the stage's byte count never depends on how narrow
+    // boxes are accounted; rows past the cache extent are zero-filled like TMA's.
+    if (ntiles > 0) {
+      if (lane == 0) {
+        prefetch_tmap(&tmK);
+        prefetch_tmap(&tmV);
       }
       bool ok = true;
       for (int t = 0; t < ntiles && ok; ++t) {
         const int s = t % NST;
-        if (t >= NST) ok = mbar_wait(&empty[s], ((t / NST) - 1) & 1);
+        if (t >= NST) ok = mbar_wait_warp(&empty[s], ((t / NST) - 1) & 1);
         if (!ok) break;
         unsigned char *st = smem + s * C::STAGE;
-        mbar_expect_tx(&full[s], C::STAGE);
         const int z = (int)(lo + t * TP - p.row_offset);
+        if (lane == 0) {
+          mbar_expect_tx(&full[s], 2 * C::KVT);
 #pragma unroll
-        for (int cb = 0; cb < C::NCB; ++cb) {
-          tma_load_4d(st + cb * TP * 128, &tmK, &full[s], cb * (128 / C::ES), (int)kvh, z, (int)b);
-          tma_load_4d(st + C::KVT + cb * TP * 128, &tmV, &full[s], cb * (128 / C::ES), (int)kvh, z, (int)b);
+          for (int cb = 0; cb < C::NCB; ++cb) {
+            tma_load_4d(st + cb * TP * 128, &tmK, &full[s], cb * (128 / C::ES), (int)kvh, z, (int)b);
+            tma_load_4d(st + C::KVT + cb * TP * 128, &tmV, &full[s], cb * (128 / C::ES), (int)kvh, z, (int)b);
+          }
         }
         if constexpr (MODE == BG_KV_Q8) {
-          tma_load_4d(st + 2 * C::KVT, &tmKs, &full[s], 0, (int)kvh, z, (int)b);
-          tma_load_4d(st + 2 * C::KVT + C::SCT, &tmVs, &full[s], 0, (int)kvh, z, (int)b);
+          constexpr int CPR = NB / 4;  // 16-byte chunks per scale row
+          const uint32_t sbase = smem_u32(st + 2 * C::KVT);
+          for (int idx = lane; idx < 2 * TP * CPR; idx += 32) {
+            const int which = idx / (TP * CPR), rem = idx % (TP * CPR);
+            const int r = rem / CPR, gc = rem % CPR;
+            const uint32_t pl = lo + t * TP + r;
+            const bool valid = pl < p.pos_hi;
+            const uint64_t row = valid ? (((uint64_t)b * p.seq_stride + (pl - p.row_offset)) * p.KV + kvh) : 0;
+            const float *src = (which ? p.Vsp : p.Ksp) + row * NB + gc * 4;
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(sbase + which * C::SCT +
+                                                                              (r * NB + gc * 4) * 4),
+                         "l"(src), "r"(valid ? 16u : 0u)
+                         : "memory");
+          }
+          asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&full[s])) : "memory");
         }
       }
-      // never leave the CTA with bulk copies in flight: wait (bounded) for the last loads
-      for (int t = max(0, ntiles - NST); t < ntiles; ++t) mbar_wait(&full[t % NST], (t / NST) & 1);
+      // never leave the CTA with copies in flight: wait (bounded) for the last stages
+      if (lane == 0)
+        for (int t = max(0, ntiles - NST); t < ntiles; ++t) mbar_wait(&full[t % NST], (t / NST) & 1);
+      asm volatile("cp.async.wait_all;" ::: "memory");
     }
     return;
   }
@@ -223,7 +289,7 @@ __global__ void __launch_bounds__(160, (MODE == BG_KV_Q8 && NT == 1 && D == 128)
   // which cancels the +1152 bias of the codes fed to the MMA.  Seeds live in shared memory
   // ([column][block], after the barriers) to keep registers for occupancy.
   float *kcorr_s = reinterpret_cast<float *>(empty + NST);
-  if constexpr (MODE == BG_KV_Q8) {
+  if constexpr (MODE == BG_KV_Q8 && !ROLL) {
     for (int idx = tid; idx < NT * 8 * NB; idx += C::NCW * 32) {
       const uint32_t rc = idx / NB, bk = idx % NB;
       float sum = 0.f;
@@ -261,7 +327,7 @@ __global__ void __launch_bounds__(160, (MODE == BG_KV_Q8 && NT == 1 && D == 128)
   bool ok = true;
   for (int t = 0; t < ntiles; ++t) {
     const int s = t % NST;
-    if (!mbar_wait(&full[s], (t / NST) & 1)) {
+    if (!mbar_wait_warp(&full[s], (t / NST) & 1)) {
       ok = false;
       break;
     }
@@ -270,9 +336,91 @@ __global__ void __launch_bounds__(160, (MODE == BG_KV_Q8 && NT == 1 && D == 128)
     const int row0 = warp * 16;
     const uint32_t pa = lo + t * TP + row0 + (lane >> 2), pb = pa + 8;
 
+
     // ---- scores S^T[pos][n] ----
     float sc[NT][4];
-    if constexpr (MODE == BG_KV_F16) {
+    if constexpr (ROLL) {
+      // rope-at-read by logical slot (attention_sg_roll.wgsl:42-50): dequantise K to f32, rotate
+      // each dim with its partner d +- D/2 (held in the same lane and register slot, KS/2 steps
+      // away), round to f16 and run the same S^T = K Q^T MMAs.
+      constexpr int HALF = D / 2;
+      const uint32_t ja = min(pa, hi - 1), jb = min(pb, hi - 1);  // masked tail rows: any valid slot
+      const float *ca = p.cosT + (uint64_t)ja * HALF, *sa_ = p.sinT + (uint64_t)ja * HALF;
+      const float *cb = p.cosT + (uint64_t)jb * HALF, *sb_ = p.sinT + (uint64_t)jb * HALF;
+      float kf[KS][8];  // per k step: {a0.x, a0.y, a1.x, a1.y, a2.x, a2.y, a3.x, a3.y}
+      if constexpr (MODE == BG_KV_F16) {
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+          uint32_t a[4];
+          ldsm_x4(a, swz<TP>(kb, row0 + lrow, 2 * ks + lhi));
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&a[i]));
+            kf[ks][2 * i] = f.x;
+            kf[ks][2 * i + 1] = f.y;
+          }
+        }
+      } else {
+        const float *ksc = reinterpret_cast<const float *>(smem + s * C::STAGE + 2 * C::KVT);
+#pragma unroll
+        for (int bk = 0; bk < NB; ++bk) {
+          uint32_t r[4];
+          ldsm_x4(r, swz<TP>(kb, row0 + lrow, 2 * bk + lhi));
+          const float s0 = ksc[(row0 + (lane >> 2)) * NB + bk] * (1.0f / 127.0f);
+          const float s1 = ksc[(row0 + (lane >> 2) + 8) * NB + bk] * (1.0f / 127.0f);
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {  // k step 2bk + h2 from words r[2h2] (row a), r[2h2+1] (row b)
+            const uint32_t wa = r[2 * h2], wb = r[2 * h2 + 1];
+            float *o = kf[2 * bk + h2];
+            // a0 = bytes 0,1 of row a; a1 = bytes 0,1 of row b; a2 = bytes 2,3 of row a; a3 = row b
+            // snorm8 read: max(code/127, -1) * scale == max(code, -127) * (scale/127)
+            o[0] = fmaxf((float)(int8_t)(wa & 0xff), -127.f) * s0;
+            o[1] = fmaxf((float)(int8_t)((wa >> 8) & 0xff), -127.f) * s0;
+            o[2] = fmaxf((float)(int8_t)(wb & 0xff), -127.f) * s1;
+            o[3] = fmaxf((float)(int8_t)((wb >> 8) & 0xff), -127.f) * s1;
+            o[4] = fmaxf((float)(int8_t)((wa >> 16) & 0xff), -127.f) * s0;
+            o[5] = fmaxf((float)(int8_t)((wa >> 24) & 0xff), -127.f) * s0;
+            o[6] = fmaxf((float)(int8_t)((wb >> 16) & 0xff), -127.f) * s1;
+            o[7] = fmaxf((float)(int8_t)((wb >> 24) & 0xff), -127.f) * s1;
+          }
+        }
+      }
+      // rotation: element e of step ks sits at dim d(ks, e); its partner is step ks + KS/2
+#pragma unroll
+      for (int ks = 0; ks < KS / 2; ++ks) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const bool rowb = (e >> 1) & 1;  // a1 / a3 hold row b
+          int dh;                          // dim within the half (d mod D/2)
+          if constexpr (MODE == BG_KV_F16) dh = ks * 16 + 2 * (lane & 3) + (e & 1) + ((e >> 2) & 1) * 8;
+          else dh = (ks >> 1) * 32 + (ks & 1) * 16 + 4 * (lane & 3) + ((e >> 2) & 1) * 2 + (e & 1);
+          const float c = rowb ? __ldg(cb + dh) : __ldg(ca + dh);
+          const float sn = rowb ? __ldg(sb_ + dh) : __ldg(sa_ + dh);
+          const float lo_v = kf[ks][e], hi_v = kf[ks + KS / 2][e];
+          kf[ks][e] = lo_v * c - hi_v * sn;          // d < D/2: k*cos + (-k[d+D/2])*sin
+          kf[ks + KS / 2][e] = hi_v * c + lo_v * sn; // d >= D/2: k*cos + k[d-D/2]*sin
+        }
+      }
+      float acc[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[nt][i] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+        const uint32_t a[4] = {pack_f16(kf[ks][0], kf[ks][1]), pack_f16(kf[ks][2], kf[ks][3]),
+                               pack_f16(kf[ks][4], kf[ks][5]), pack_f16(kf[ks][6], kf[ks][7])};
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          mma16816(acc[nt], a, qh[nt][ks][0], qh[nt][ks][1]);
+          mma16816(acc[nt], a, ql[nt][ks][0], ql[nt][ks][1]);
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sc[nt][i] = acc[nt][i] * p.sl2;
+    } else if constexpr (MODE == BG_KV_F16) {
       float acc[NT][4];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
@@ -487,10 +635,11 @@ __global__ void __launch_bounds__(160, (MODE == BG_KV_Q8 && NT == 1 && D == 128)
   }
 }
 
-template <int MODE, int D, int NT>
+template <int MODE, int D, int NT, bool ROLL>
 int launch_cfg(const AttnArgs &a, cudaStream_t st) {
   using C = Cfg<MODE, D>;
   CUtensorMap tk, tv, tks, tvs;
+  if (!ROLL) {
   const uint64_t Lvalid = a.pos_hi - a.kv.row_offset;
   const uint64_t dims[4] = {a.D, a.KV, Lvalid, a.B};
   const uint64_t rb = (uint64_t)a.D * C::ES;
@@ -499,18 +648,11 @@ int launch_cfg(const AttnArgs &a, cudaStream_t st) {
   const CUtensorMapDataType dt = MODE == BG_KV_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   if (make_tmap_4d(&tk, dt, a.kv.K, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) return BG_EUNSUPPORTED;
   if (make_tmap_4d(&tv, dt, a.kv.V, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) return BG_EUNSUPPORTED;
-  if constexpr (MODE == BG_KV_Q8) {
-    const uint64_t sd[4] = {C::NB, a.KV, Lvalid, a.B};
-    const uint64_t sr = (uint64_t)C::NB * 4;
-    const uint64_t ss[3] = {sr, sr * a.KV, sr * a.KV * a.kv.seq_stride};
-    const uint32_t sbx[4] = {C::NB, 1, C::TP, 1};
-    if (make_tmap_4d(&tks, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.kv.Ks, sd, ss, sbx, CU_TENSOR_MAP_SWIZZLE_NONE))
-      return BG_EUNSUPPORTED;
-    if (make_tmap_4d(&tvs, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.kv.Vs, sd, ss, sbx, CU_TENSOR_MAP_SWIZZLE_NONE))
-      return BG_EUNSUPPORTED;
+  tks = tk;  // the q8 block scales travel by cp.async (see the producer), not TMA
+  tvs = tv;
   } else {
-    tks = tk;
-    tvs = tv;
+    memset(&tk, 0, sizeof(tk));  // the cp.async producer of the ROLL kernels uses no tensor map
+    tv = tks = tvs = tk;
   }
   TcParams p;
   p.q = a.q;
@@ -532,20 +674,30 @@ int launch_cfg(const AttnArgs &a, cudaStream_t st) {
   p.out = a.out;
   p.out_f16 = a.out_f16;
   p.gate = a.gate;
-  auto kern = attn_tc_kernel<MODE, D, NT>;
+  p.cosT = a.cosT;
+  p.sinT = a.sinT;
+  p.Kp = static_cast<const unsigned char *>(a.kv.K);
+  p.Vp = static_cast<const unsigned char *>(a.kv.V);
+  p.Ksp = a.kv.Ks;
+  p.Vsp = a.kv.Vs;
+  p.seq_stride = a.kv.seq_stride;
+  p.sinks = a.kv.sinks;
+  p.window = a.kv.window;
+  p.ring_head = a.kv.ring_head;
+  auto kern = attn_tc_kernel<MODE, D, NT, ROLL>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
     return BG_ELAUNCH;
   kern<<<dim3(a.nsplit, a.B * a.KV), 160, C::SMEM, st>>>(tk, tv, tks, tvs, p);
   return cudaGetLastError() == cudaSuccess ? BG_OK : BG_ELAUNCH;
 }
 
-template <int MODE, int D, int NT>
+template <int MODE, int D, int NT, bool ROLL = false>
 int occupancy() {
   using C = Cfg<MODE, D>;
   static int cached = 0;
   if (!cached) {
     int n = 0;
-    auto kern = attn_tc_kernel<MODE, D, NT>;
+    auto kern = attn_tc_kernel<MODE, D, NT, ROLL>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, 160, C::SMEM) != cudaSuccess || n < 1) n = 1;
     cached = n;
@@ -555,23 +707,32 @@ int occupancy() {
 
 template <int MODE>
 int launch_mode(const AttnArgs &a, uint32_t M, cudaStream_t st) {
-  if (a.D == 128) return M <= 8 ? launch_cfg<MODE, 128, 1>(a, st) : launch_cfg<MODE, 128, 2>(a, st);
-  if (a.D == 256 && M <= 8) return launch_cfg<MODE, 256, 1>(a, st);
+  const bool roll = a.cosT != nullptr || a.kv.window != 0;
+  if (roll) {
+    if (a.D != 128 || !a.cosT) return BG_EUNSUPPORTED;  // ring without rope-at-read: generic path
+    return M <= 8 ? launch_cfg<MODE, 128, 1, true>(a, st) : launch_cfg<MODE, 128, 2, true>(a, st);
+  }
+  if (a.D == 128) return M <= 8 ? launch_cfg<MODE, 128, 1, false>(a, st) : launch_cfg<MODE, 128, 2, false>(a, st);
+  if (a.D == 256 && M <= 8) return launch_cfg<MODE, 256, 1, false>(a, st);
   return BG_EUNSUPPORTED;
 }
 
 }  // namespace
 
 bool attn_tc_supported(int mode, uint32_t D, uint32_t S, uint32_t H, uint32_t KV, bool roll, bool ring) {
-  if (roll || ring) return false;  // rope-at-read / ring mapping: generic path
   if (mode != BG_KV_F16 && mode != BG_KV_Q8) return false;
   const uint32_t M = S * (H / KV);
+  if (roll || ring) return roll && D == 128 && M <= 16;  // rope-at-read kernels (cp.async producer)
   if (D == 128) return M <= 16;
   if (D == 256) return M <= 8;
   return false;
 }
 
-int attn_tc_ctas_per_sm(int mode, uint32_t D, uint32_t M) {
+int attn_tc_ctas_per_sm(int mode, uint32_t D, uint32_t M, bool roll) {
+  if (roll) {
+    if (mode == BG_KV_F16) return M <= 8 ? occupancy<BG_KV_F16, 128, 1, true>() : occupancy<BG_KV_F16, 128, 2, true>();
+    return M <= 8 ? occupancy<BG_KV_Q8, 128, 1, true>() : occupancy<BG_KV_Q8, 128, 2, true>();
+  }
   if (mode == BG_KV_F16) {
     if (D == 256) return occupancy<BG_KV_F16, 256, 1>();
     return M <= 8 ? occupancy<BG_KV_F16, 128, 1>() : occupancy<BG_KV_F16, 128, 2>();

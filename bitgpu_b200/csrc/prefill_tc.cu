@@ -288,7 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
-      if (!mbar_wait(&s_full[t], j & 1)) { ok = false; break; }
+      if (!mbar_wait_warp(&s_full[t], j & 1)) { ok = false; break; }
       tc_fence_after();
       const uint32_t sbase = tS[t] | lane_off;
       const int key0 = j * kKeys;
@@ -378,7 +378,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(&p_full[t]);
     }
     // epilogue: wait for the last PV of this tile, then O / l -> out
-    if (ok && ntiles > 0 && mbar_wait(&o_done[t], (ntiles - 1) & 1)) {
+    if (ok && ntiles > 0 && mbar_wait_warp(&o_done[t], (ntiles - 1) & 1)) {
       tc_fence_after();
       const uint32_t obase = tO[t] | lane_off;
       const float inv = 1.0f / l;

@@ -51,6 +51,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
   return false;
 }
 
+// Whole-warp form: every lane polls, then the warp reconverges (__all_sync) before the
+// .sync.aligned instructions that follow (ldmatrix, mma.sync, movmatrix, tcgen05.ld/st), and the
+// timeout decision is the same on every lane.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity) {
+  const bool ok = mbar_wait(bar, parity);
+  return __all_sync(0xffffffffu, ok);
+}
+
 __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y, int z,
                                             int w) {
   asm volatile(

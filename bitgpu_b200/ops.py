@@ -222,3 +222,29 @@ def gate_sigmoid(x, gate):
     y = torch.empty_like(x)
     check("bg_gate_sigmoid", lib().bg_gate_sigmoid(_p(x), _p(gate), x.numel(), _p(y), _stream()))
     return y
+
+
+class Graphed:
+    """Capture a sequence of these ops once as a CUDA graph and replay it.
+
+    Decode steps of the small layers (one DeltaNet token, a short-context attention) are a few
+    microseconds of GPU work behind tens of microseconds of host launch overhead; replaying a
+    captured graph removes the host from the per-step path.  Inputs and outputs must live in
+    fixed buffers (copy new inputs into them before ``replay``)."""
+
+    def __init__(self, fn, warmup=2):
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(warmup):
+                fn()
+        torch.cuda.current_stream().wait_stream(s)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out = fn()
+
+    def replay(self):
+        self.graph.replay()
+        return self.out
+
+    __call__ = replay

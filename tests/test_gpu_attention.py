@@ -195,3 +195,30 @@ def test_tc_oracle_spot(ops):
     """Tensor-core path vs oracle at the config-2 shape (2 sequences sampled)."""
     for mode in ("f16", "q8"):
         run_case(ops, mode, B=2, S=1, H=32, KV=8, D=128, pos_base=32767, seed=31)
+
+
+@pytest.mark.parametrize("mode", ["f16", "q8"])
+@pytest.mark.parametrize("S,ring_head", [(1, 0), (1, 1500), (2, 4090), (3, 77)])
+def test_roll_tensor_core_vs_generic(ops, mode, S, ring_head):
+    """Rope-at-read on the tensor cores (cp.async ring producer, rotation in registers) vs the
+    CUDA-core kernel, on a ring whose wrap point falls inside tiles."""
+    from bitgpu_b200._lib import lib
+    B, H, KV, D, SINKS, W = 3, 16, 8, 128, 4, 4096
+    g = torch.Generator(device="cuda").manual_seed(S + ring_head)
+    cache = ops.KVCache(B, 0, KV, D, mode=mode, sinks=SINKS, window=W)
+    cache.ring_head = ring_head
+    L = SINKS + W - 5
+    cache.append(0, torch.randn((B, L, KV, D), generator=g, device="cuda"), 0)
+    cache.append(1, torch.randn((B, L, KV, D), generator=g, device="cuda"), 0)
+    c, s_ = OR.synth_rope(D, SINKS + W, 1e6, "yarn", 4.0, 8192)
+    cos_t, sin_t = torch.from_numpy(c).cuda(), torch.from_numpy(s_).cuda()
+    q = torch.randn((B, S, H, D), generator=g, device="cuda")
+    a = ops.attention(q, cache, L - S, cos_t=cos_t, sin_t=sin_t)
+    prev = lib().bg_force_generic(1)
+    try:
+        b = ops.attention(q, cache, L - S, cos_t=cos_t, sin_t=sin_t)
+    finally:
+        lib().bg_force_generic(prev)
+    err = (a - b).abs().max().item()
+    assert err < 1e-3, err
+    assert lib().bg_device_status(None) == 0
