@@ -159,12 +159,23 @@ __global__ void __launch_bounds__(160, (MODE == BG_KV_Q8 && NT == 1 && D == 128 
       if (!ok) break;
       const uint32_t st = smem_u32(smem + s * C::STAGE);
       const uint32_t p0 = lo + t * TP;
+      // physical row of tile rows `lane` and `lane + 32` (ring offset < 2*window: one subtraction)
+      uint32_t phr[2];
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const uint32_t pl = p0 + lane + 32 * h2;
+        uint32_t ph = pl - p.row_offset;
+        if (p.window && pl >= p.sinks) {
+          uint32_t rel = p.ring_head + (pl - p.sinks);
+          if (rel >= p.window) rel -= p.window;
+          ph = p.sinks + rel;
+        }
+        phr[h2] = ph;
+      }
       for (int idx = lane; idx < TP * CPR; idx += 32) {
         const int r = idx / CPR, gc = idx % CPR;
-        const uint32_t pl = p0 + r;
-        const bool valid = pl < hi;
-        uint32_t ph = pl - p.row_offset;
-        if (p.window && pl >= p.sinks) ph = p.sinks + (p.ring_head + (pl - p.sinks)) % p.window;
+        const uint32_t ph = __shfl_sync(0xffffffffu, phr[r >> 5], r & 31);
+        const bool valid = p0 + r < hi;
         const uint64_t row = valid ? (((uint64_t)b * p.seq_stride + ph) * p.KV + kvh) : 0;
         const unsigned char *srcK = p.Kp + row * C::ROWB + gc * 16;
         const unsigned char *srcV = p.Vp + row * C::ROWB + gc * 16;
@@ -385,17 +396,39 @@ __global__ void __launch_bounds__(160, (MODE == BG_KV_Q8 && NT == 1 && D == 128 
           }
         }
       }
-      // rotation: element e of step ks sits at dim d(ks, e); its partner is step ks + KS/2
+      // rotation: element e of step ks sits at dim d(ks, e); its partner is step ks + KS/2.
+      // cos/sin come as vectors: q8 steps hold 4 consecutive dims per row (float4), f16 steps two
+      // pairs 8 dims apart (float2 x 2).
 #pragma unroll
       for (int ks = 0; ks < KS / 2; ++ks) {
+        float cr_[2][4], sr_[2][4];  // [row a/b][dim slot]
+        if constexpr (MODE == BG_KV_F16) {
+          const int d0 = ks * 16 + 2 * (lane & 3);
+#pragma unroll
+          for (int rb = 0; rb < 2; ++rb) {
+            const float *cc = rb ? cb : ca, *ss = rb ? sb_ : sa_;
+            const float2 c0 = __ldg(reinterpret_cast<const float2 *>(cc + d0));
+            const float2 c1 = __ldg(reinterpret_cast<const float2 *>(cc + d0 + 8));
+            const float2 s0 = __ldg(reinterpret_cast<const float2 *>(ss + d0));
+            const float2 s1 = __ldg(reinterpret_cast<const float2 *>(ss + d0 + 8));
+            cr_[rb][0] = c0.x; cr_[rb][1] = c0.y; cr_[rb][2] = c1.x; cr_[rb][3] = c1.y;
+            sr_[rb][0] = s0.x; sr_[rb][1] = s0.y; sr_[rb][2] = s1.x; sr_[rb][3] = s1.y;
+          }
+        } else {
+          const int d0 = (ks >> 1) * 32 + (ks & 1) * 16 + 4 * (lane & 3);
+#pragma unroll
+          for (int rb = 0; rb < 2; ++rb) {
+            const float4 c4 = __ldg(reinterpret_cast<const float4 *>((rb ? cb : ca) + d0));
+            const float4 s4 = __ldg(reinterpret_cast<const float4 *>((rb ? sb_ : sa_) + d0));
+            cr_[rb][0] = c4.x; cr_[rb][1] = c4.y; cr_[rb][2] = c4.z; cr_[rb][3] = c4.w;
+            sr_[rb][0] = s4.x; sr_[rb][1] = s4.y; sr_[rb][2] = s4.z; sr_[rb][3] = s4.w;
+          }
+        }
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          const bool rowb = (e >> 1) & 1;  // a1 / a3 hold row b
-          int dh;                          // dim within the half (d mod D/2)
-          if constexpr (MODE == BG_KV_F16) dh = ks * 16 + 2 * (lane & 3) + (e & 1) + ((e >> 2) & 1) * 8;
-          else dh = (ks >> 1) * 32 + (ks & 1) * 16 + 4 * (lane & 3) + ((e >> 2) & 1) * 2 + (e & 1);
-          const float c = rowb ? __ldg(cb + dh) : __ldg(ca + dh);
-          const float sn = rowb ? __ldg(sb_ + dh) : __ldg(sa_ + dh);
+          const int rb = (e >> 1) & 1;                    // a1 / a3 hold row b
+          const int slot = ((e >> 2) & 1) * 2 + (e & 1);  // dim slot within the vectors above
+          const float c = cr_[rb][slot], sn = sr_[rb][slot];
           const float lo_v = kf[ks][e], hi_v = kf[ks + KS / 2][e];
           kf[ks][e] = lo_v * c - hi_v * sn;          // d < D/2: k*cos + (-k[d+D/2])*sin
           kf[ks + KS / 2][e] = hi_v * c + lo_v * sn; // d >= D/2: k*cos + k[d-D/2]*sin
