@@ -25,6 +25,7 @@ import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
+os.environ["NCCL_DEBUG"] = os.environ.get("BENCH_NCCL_DEBUG", "WARN")  # stdout carries only the JSON line
 
 # config 2; manifest models/bonsai-8b-gguf: heads 32, kv_heads 8, head_dim 128
 B, L, H, KV, D = 64, 32768, 32, 8, 128
@@ -319,7 +320,9 @@ def run_gated(torch, ops, args, ws, rank, barrier, max_over_ranks):
         fn = lambda: ops.attention(q, cache, L - 1, scale=scale, gate=gate, out=out)
         launches = 1
     else:
-        fn = lambda: dec.step(q, cache, L - 1, gate=gate, scale=scale)
+        # the whole step -- partials kernel, NCCL all-gather, merge kernel -- replayed as one CUDA
+        # graph, so the host adds nothing per step
+        fn = ops.Graphed(lambda: dec.step(q, cache, L - 1, gate=gate, scale=scale))
         launches = 2
     ms = max_over_ranks(time_steps(torch, fn, args.steps, args.warmup, barrier))
     byts = 2 * L * GA_KV * GA_D * 2 + 3 * GA_H * GA_D * 4
@@ -441,7 +444,7 @@ def run_ours(args):
     dist = None
     if ws > 1:
         import torch.distributed as dist
-        dist.init_process_group("nccl")
+        dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local}"))
     barrier = (lambda: dist.barrier()) if dist else (lambda: None)
     from bitgpu_b200 import ops
     hbm, bf16_peak, peak_kind = peaks()

@@ -178,49 +178,73 @@ __global__ void __launch_bounds__(128) attn_generic_kernel(AttnArgs a) {
   }
 }
 
-// Combine split partials [nsplit][rows][D+2] -> out[rows][D], optional sigmoid gate.
+// Combine split partials [nsplit][rows][D+2] -> out[rows][D], optional sigmoid gate (or, with
+// out_f16 < 0, into one partial row (o, m, l) for split-KV slices).  One block per row: the split
+// weights exp(m_s - M) are computed in parallel with block reductions, then thread (d, group)
+// sums a strided subset of the splits for dim d and the groups are added in shared memory.
+__device__ __forceinline__ float block_reduce(float v, float *scratch, bool is_max) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float x = __shfl_xor_sync(0xffffffffu, v, o);
+    v = is_max ? fmaxf(v, x) : v + x;
+  }
+  __syncthreads();
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  float r = is_max ? -INFINITY : 0.f;
+  for (int w = 0; w < nw; ++w) r = is_max ? fmaxf(r, scratch[w]) : r + scratch[w];
+  return r;
+}
+
 __global__ void lse_merge_kernel(const float *__restrict__ part, uint32_t nsplit, uint32_t rows,
                                  uint32_t D, const float *__restrict__ gate, void *out, int out_f16) {
   const uint32_t row = blockIdx.x;
-  extern __shared__ float w[];  // [nsplit] weights, then total
-  __shared__ float Ltot, Mx;
-  if (threadIdx.x == 0) {
-    float M = -INFINITY;
-    for (uint32_t s = 0; s < nsplit; ++s) {
-      const float *p = part + ((uint64_t)s * rows + row) * (D + 2);
-      if (p[D + 1] > 0.f) M = fmaxf(M, p[D]);
+  extern __shared__ float sm[];  // [nsplit] weights, then [groups][D] partial sums
+  float *w = sm;
+  float *acc = sm + nsplit;
+  __shared__ float red[32];
+  const uint64_t stride = (uint64_t)rows * (D + 2);
+  const float *base = part + (uint64_t)row * (D + 2);
+  float M = -INFINITY;
+  for (uint32_t s = threadIdx.x; s < nsplit; s += blockDim.x)
+    if (base[s * stride + D + 1] > 0.f) M = fmaxf(M, base[s * stride + D]);
+  M = block_reduce(M, red, true);
+  float L = 0.f;
+  for (uint32_t s = threadIdx.x; s < nsplit; s += blockDim.x) {
+    const float l = base[s * stride + D + 1];
+    const float f = l > 0.f ? expf(base[s * stride + D] - M) : 0.f;
+    w[s] = f;
+    L = fmaf(l, f, L);
+  }
+  L = block_reduce(L, red, false);  // (its barriers also publish w[])
+  const uint32_t groups = blockDim.x / D;
+  const uint32_t d = threadIdx.x % D, g = threadIdx.x / D;
+  if (g < groups) {
+    float o = 0.f;
+    for (uint32_t s = g; s < nsplit; s += groups) {
+      const float f = w[s];
+      if (f != 0.f) o = fmaf(base[s * stride + d], f, o);
     }
-    float L = 0.f;
-    for (uint32_t s = 0; s < nsplit; ++s) {
-      const float *p = part + ((uint64_t)s * rows + row) * (D + 2);
-      const float f = p[D + 1] > 0.f ? expf(p[D] - M) : 0.f;
-      w[s] = f;
-      L = fmaf(p[D + 1], f, L);
-    }
-    Ltot = L;
-    Mx = M;
+    acc[g * D + d] = o;
   }
   __syncthreads();
-  for (uint32_t d = threadIdx.x; d < D; d += blockDim.x) {
-    float o = 0.f;
-    for (uint32_t s = 0; s < nsplit; ++s) {
-      const float f = w[s];
-      if (f != 0.f) o = fmaf(part[((uint64_t)s * rows + row) * (D + 2) + d], f, o);
+  if (threadIdx.x >= D) return;
+  float o = 0.f;
+  for (uint32_t k = 0; k < groups; ++k) o += acc[k * D + d];
+  if (out_f16 < 0) {
+    float *dst = static_cast<float *>(out) + (uint64_t)row * (D + 2);
+    dst[d] = o;
+    if (d == 0) {
+      dst[D] = L > 0.f ? M : -INFINITY;
+      dst[D + 1] = L;
     }
-    if (out_f16 < 0) {  // merge into one partial row (o, m, l): used by split-KV slices
-      float *dst = static_cast<float *>(out) + (uint64_t)row * (D + 2);
-      dst[d] = o;
-      if (d == 0) {
-        dst[D] = Ltot > 0.f ? Mx : -INFINITY;
-        dst[D + 1] = Ltot;
-      }
-      continue;
-    }
-    o = o / Ltot;
-    if (gate) o = o / (1.0f + expf(-gate[(uint64_t)row * D + d]));
-    if (out_f16) static_cast<__half *>(out)[(uint64_t)row * D + d] = __float2half_rn(o);
-    else static_cast<float *>(out)[(uint64_t)row * D + d] = o;
+    return;
   }
+  o = o / L;
+  if (gate) o = o / (1.0f + expf(-gate[(uint64_t)row * D + d]));
+  if (out_f16) static_cast<__half *>(out)[(uint64_t)row * D + d] = __float2half_rn(o);
+  else static_cast<float *>(out)[(uint64_t)row * D + d] = o;
 }
 
 template <int MODE, int D, bool ROLL>
@@ -382,8 +406,17 @@ int launch_attn_generic(const AttnArgs &a, cudaStream_t st) {
 int launch_lse_merge(const float *partials, uint32_t nsplit, uint32_t rows, uint32_t D,
                      const float *gate, void *out, int out_f16, cudaStream_t st) {
   if (rows == 0) return BG_OK;
-  const int threads = D >= 128 ? 128 : 64;
-  lse_merge_kernel<<<rows, threads, nsplit * sizeof(float), st>>>(partials, nsplit, rows, D, gate, out, out_f16);
+  if (D > 1024) return BG_EUNSUPPORTED;
+  // as many split groups as fit 1024 threads, but no more than there are splits
+  uint32_t groups = 1024 / D;
+  if (groups > nsplit) groups = nsplit;
+  if (groups < 1) groups = 1;
+  const uint32_t threads = ((groups * D + 31) / 32) * 32;
+  const size_t smem = (size_t)(nsplit + groups * D) * sizeof(float);
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(lse_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return BG_EUNSUPPORTED;
+  lse_merge_kernel<<<rows, threads, smem, st>>>(partials, nsplit, rows, D, gate, out, out_f16);
   return cudaGetLastError() == cudaSuccess ? BG_OK : BG_ELAUNCH;
 }
 
