@@ -18,7 +18,8 @@ EXPORTS = [
     "bg_strerror", "bg_version", "bg_device_status", "bg_force_generic", "bg_attention_workspace_size", "bg_attention", "bg_attention_partials",
     "bg_lse_merge", "bg_kv_append", "bg_rmsnorm_rope", "bg_kv_evict", "bg_kv_ring_evict",
     "bg_deltanet_gbeta", "bg_deltanet_recur", "bg_deltanet_norm_gate", "bg_deltanet_fused",
-    "bg_gate_sigmoid", "bg_attention_noalloc",
+    "bg_gate_sigmoid", "bg_attention_noalloc", "bg_deltanet_chunked_workspace_size",
+    "bg_deltanet_chunked",
 ]
 
 
@@ -62,6 +63,8 @@ _SIGS = {
     "bg_deltanet_norm_gate": (C.c_int, [P, P, P, U32, U32, F, P, P]),
     "bg_deltanet_fused": (C.c_int, [U32, U32, U32, U32, U32, P, P, P, P, P, P, P, P, P, F, P, P, P, P, P]),
     "bg_gate_sigmoid": (C.c_int, [P, P, U32, P, P]),
+    "bg_deltanet_chunked_workspace_size": (SZ, [U32, U32, U32, U32]),
+    "bg_deltanet_chunked": (C.c_int, [U32, U32, U32, U32, U32, P, P, P, P, P, P, P, P, P, F, P, P, P, P, P, SZ, P]),
     "bg_attention_noalloc": (C.c_int, [C.POINTER(AttnParams), U32, P, U32, C.POINTER(KVCacheDesc), P, P, F, P, P,
                                        U32, P]),
 }

@@ -367,6 +367,41 @@ int bg_deltanet_fused(uint32_t S, uint32_t H, uint32_t HK, uint32_t DK, uint32_t
   return launch_deltanet(d, (cudaStream_t)stream);
 }
 
+size_t bg_deltanet_chunked_workspace_size(uint32_t S, uint32_t H, uint32_t DK, uint32_t DV) {
+  if (DK != 128 || DV != 128) return 0;
+  return deltanet_chunk_workspace(S, H);
+}
+
+int bg_deltanet_chunked(uint32_t S, uint32_t H, uint32_t HK, uint32_t DK, uint32_t DV, const float *q, const float *k,
+                        const float *v, const float *a, const float *b, const float *a_neg, const float *dt_bias,
+                        const float *z, const float *gamma, float eps, const float *state_in, float *state_out,
+                        float *core, float *y, void *workspace, size_t workspace_bytes, bg_stream_t stream) {
+  if (!q || !k || !v || !a || !b || !a_neg || !dt_bias || !z || !gamma || !y || !state_out || !core) return BG_EINVAL;
+  if (!H || !HK || H % HK) return BG_EINVAL;
+  if (DK != 128 || DV != 128) return BG_EUNSUPPORTED;
+  DeltaArgs d = {};
+  d.S = S;
+  d.H = H;
+  d.HK = HK;
+  d.DK = DK;
+  d.DV = DV;
+  d.loadState = state_in != nullptr;
+  d.q = q;
+  d.k = k;
+  d.v = v;
+  d.a = a;
+  d.b = b;
+  d.a_neg = a_neg;
+  d.dt_bias = dt_bias;
+  d.state_in = state_in;
+  d.state_out = state_out;
+  d.core = core;
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc = launch_deltanet_chunked(d, workspace, workspace_bytes, st);
+  if (rc || S == 0) return rc;
+  return launch_norm_gate(core, z, gamma, S * H, DV, eps, y, st);  // deltanet_norm_gate.wgsl
+}
+
 int bg_gate_sigmoid(const float *x, const float *gate, uint32_t n, float *y, bg_stream_t stream) {
   if (!x || !gate || !y) return BG_EINVAL;
   return launch_gate_sigmoid(x, gate, n, y, (cudaStream_t)stream);

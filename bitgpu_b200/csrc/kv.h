@@ -26,6 +26,8 @@ struct DeltaArgs {
 };
 
 int launch_deltanet(const DeltaArgs &a, cudaStream_t st);
+size_t deltanet_chunk_workspace(uint32_t S, uint32_t H);
+int launch_deltanet_chunked(const DeltaArgs &a, void *ws, size_t ws_bytes, cudaStream_t st);
 int launch_gbeta(const float *a, const float *b, const float *a_neg, const float *dt, uint32_t S, uint32_t H,
                  float *out, cudaStream_t st);
 int launch_norm_gate(const float *core, const float *z, const float *gamma, uint32_t rows, uint32_t DV, float eps,

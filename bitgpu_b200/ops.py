@@ -218,6 +218,24 @@ def deltanet_fused(q, k, v, a, b, a_neg, dt_bias, z, gamma, eps, state_in=None, 
     return y, state_out, core
 
 
+def deltanet_chunked(q, k, v, a, b, a_neg, dt_bias, z, gamma, eps, state_in=None, state_out=None):
+    """Prefill form of ``deltanet_fused``: the chunk-parallel (WY, 64-token chunks) delta rule,
+    then the gated RMSNorm.  Returns ``(y, state_out, core)``."""
+    S, HK, DK = q.shape
+    H, DV = v.shape[1], v.shape[2]
+    if state_out is None:
+        state_out = torch.empty((H, DK, DV), dtype=torch.float32, device=q.device)
+    y = torch.empty((S, H, DV), dtype=torch.float32, device=q.device)
+    core = torch.empty_like(y)
+    nbytes = lib().bg_deltanet_chunked_workspace_size(S, H, DK, DV)
+    ws = WORKSPACE.get(nbytes, q.device)
+    check("bg_deltanet_chunked", lib().bg_deltanet_chunked(S, H, HK, DK, DV, _p(q), _p(k), _p(v), _p(a), _p(b),
+                                                            _p(a_neg), _p(dt_bias), _p(z), _p(gamma), float(eps),
+                                                            _p(state_in), _p(state_out), _p(core), _p(y), _p(ws),
+                                                            ws.numel(), _stream()))
+    return y, state_out, core
+
+
 def gate_sigmoid(x, gate):
     y = torch.empty_like(x)
     check("bg_gate_sigmoid", lib().bg_gate_sigmoid(_p(x), _p(gate), x.numel(), _p(y), _stream()))

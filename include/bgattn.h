@@ -165,6 +165,18 @@ int bg_deltanet_fused(uint32_t S, uint32_t H, uint32_t HK, uint32_t DK, uint32_t
                       const float *gamma, float eps, const float *state_in, float *state_out,
                       float *core, float *y, bg_stream_t stream);
 
+/* bg_deltanet_chunked: the same segment computed in the chunk-parallel WY form of
+ * tools/qwen35_numpy.py:144-187 (_delta_chunk; chunks of 64 tokens; equal to the recurrence up to
+ * f32 accumulation order), for prefill.  Same arguments as bg_deltanet_fused plus a workspace of
+ * bg_deltanet_chunked_workspace_size(S, H, DK, DV) bytes; DK = DV = 128 only. */
+size_t bg_deltanet_chunked_workspace_size(uint32_t S, uint32_t H, uint32_t DK, uint32_t DV);
+int bg_deltanet_chunked(uint32_t S, uint32_t H, uint32_t HK, uint32_t DK, uint32_t DV,
+                        const float *q, const float *k, const float *v, const float *a,
+                        const float *b, const float *a_neg, const float *dt_bias, const float *z,
+                        const float *gamma, float eps, const float *state_in, float *state_out,
+                        float *core, float *y, void *workspace, size_t workspace_bytes,
+                        bg_stream_t stream);
+
 /* bg_gate_sigmoid: gate_sigmoid.wgsl (engine.ts:1491), y = x / (1 + exp(-gate)). */
 int bg_gate_sigmoid(const float *x, const float *gate, uint32_t n, float *y, bg_stream_t stream);
 
