@@ -25,6 +25,11 @@
 #include "attn.h"
 #include "tma.cuh"
 
+// CTAs per SM the q8 rope-at-read kernel is compiled for (3: 128 registers, a few spills)
+#ifndef BG_ROLL_Q8_MINB
+#define BG_ROLL_Q8_MINB 3
+#endif
+
 namespace bg {
 namespace {
 
@@ -117,7 +122,7 @@ __device__ __forceinline__ uint32_t swz(uint32_t base, int row, int gc) {
 }
 
 template <int MODE, int D, int NT, bool ROLL>
-__global__ void __launch_bounds__(160, (MODE == BG_KV_Q8 && NT == 1 && D == 128 && !ROLL) ? 3 : 1) attn_tc_kernel(
+__global__ void __launch_bounds__(160, (MODE == BG_KV_Q8 && NT == 1 && D == 128 && !ROLL) ? 3 : (ROLL && NT == 1 ? (MODE == BG_KV_Q8 ? BG_ROLL_Q8_MINB : 2) : 1)) attn_tc_kernel(
                                                       const __grid_constant__ CUtensorMap tmK,
                                                       const __grid_constant__ CUtensorMap tmV,
                                                       const __grid_constant__ CUtensorMap tmKs,
@@ -358,49 +363,16 @@ __global__ void __launch_bounds__(160, (MODE == BG_KV_Q8 && NT == 1 && D == 128 
       const uint32_t ja = min(pa, hi - 1), jb = min(pb, hi - 1);  // masked tail rows: any valid slot
       const float *ca = p.cosT + (uint64_t)ja * HALF, *sa_ = p.sinT + (uint64_t)ja * HALF;
       const float *cb = p.cosT + (uint64_t)jb * HALF, *sb_ = p.sinT + (uint64_t)jb * HALF;
-      float kf[KS][8];  // per k step: {a0.x, a0.y, a1.x, a1.y, a2.x, a2.y, a3.x, a3.y}
-      if constexpr (MODE == BG_KV_F16) {
+      // Dims d and d + D/2 of a row sit in k steps ks and ks + KS/2 of the same lane and register
+      // slot, so each pair of steps is dequantised, rotated, packed and multiplied before the next
+      // pair is touched (keeps ~32 live floats instead of the whole row fragment).
+      float acc[NT][4];
 #pragma unroll
-        for (int ks = 0; ks < KS; ++ks) {
-          uint32_t a[4];
-          ldsm_x4(a, swz<TP>(kb, row0 + lrow, 2 * ks + lhi));
+      for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&a[i]));
-            kf[ks][2 * i] = f.x;
-            kf[ks][2 * i + 1] = f.y;
-          }
-        }
-      } else {
-        const float *ksc = reinterpret_cast<const float *>(smem + s * C::STAGE + 2 * C::KVT);
-#pragma unroll
-        for (int bk = 0; bk < NB; ++bk) {
-          uint32_t r[4];
-          ldsm_x4(r, swz<TP>(kb, row0 + lrow, 2 * bk + lhi));
-          const float s0 = ksc[(row0 + (lane >> 2)) * NB + bk] * (1.0f / 127.0f);
-          const float s1 = ksc[(row0 + (lane >> 2) + 8) * NB + bk] * (1.0f / 127.0f);
-#pragma unroll
-          for (int h2 = 0; h2 < 2; ++h2) {  // k step 2bk + h2 from words r[2h2] (row a), r[2h2+1] (row b)
-            const uint32_t wa = r[2 * h2], wb = r[2 * h2 + 1];
-            float *o = kf[2 * bk + h2];
-            // a0 = bytes 0,1 of row a; a1 = bytes 0,1 of row b; a2 = bytes 2,3 of row a; a3 = row b
-            // snorm8 read: max(code/127, -1) * scale == max(code, -127) * (scale/127)
-            o[0] = fmaxf((float)(int8_t)(wa & 0xff), -127.f) * s0;
-            o[1] = fmaxf((float)(int8_t)((wa >> 8) & 0xff), -127.f) * s0;
-            o[2] = fmaxf((float)(int8_t)(wb & 0xff), -127.f) * s1;
-            o[3] = fmaxf((float)(int8_t)((wb >> 8) & 0xff), -127.f) * s1;
-            o[4] = fmaxf((float)(int8_t)((wa >> 16) & 0xff), -127.f) * s0;
-            o[5] = fmaxf((float)(int8_t)((wa >> 24) & 0xff), -127.f) * s0;
-            o[6] = fmaxf((float)(int8_t)((wb >> 16) & 0xff), -127.f) * s1;
-            o[7] = fmaxf((float)(int8_t)((wb >> 24) & 0xff), -127.f) * s1;
-          }
-        }
-      }
-      // rotation: element e of step ks sits at dim d(ks, e); its partner is step ks + KS/2.
-      // cos/sin come as vectors: q8 steps hold 4 consecutive dims per row (float4), f16 steps two
-      // pairs 8 dims apart (float2 x 2).
-#pragma unroll
-      for (int ks = 0; ks < KS / 2; ++ks) {
+        for (int i = 0; i < 4; ++i) acc[nt][i] = 0.f;
+      // element e of a step: {a0.x, a0.y, a1.x, a1.y, a2.x, a2.y, a3.x, a3.y}; a1/a3 hold row b
+      auto rotate_mma = [&](float (&lo_f)[8], float (&hi_f)[8], int ks) {
         float cr_[2][4], sr_[2][4];  // [row a/b][dim slot]
         if constexpr (MODE == BG_KV_F16) {
           const int d0 = ks * 16 + 2 * (lane & 3);
@@ -424,29 +396,78 @@ __global__ void __launch_bounds__(160, (MODE == BG_KV_Q8 && NT == 1 && D == 128 
             sr_[rb][0] = s4.x; sr_[rb][1] = s4.y; sr_[rb][2] = s4.z; sr_[rb][3] = s4.w;
           }
         }
+        float rl[8], rh[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          const int rb = (e >> 1) & 1;                    // a1 / a3 hold row b
-          const int slot = ((e >> 2) & 1) * 2 + (e & 1);  // dim slot within the vectors above
+          const int rb = (e >> 1) & 1;
+          const int slot = ((e >> 2) & 1) * 2 + (e & 1);
           const float c = cr_[rb][slot], sn = sr_[rb][slot];
-          const float lo_v = kf[ks][e], hi_v = kf[ks + KS / 2][e];
-          kf[ks][e] = lo_v * c - hi_v * sn;          // d < D/2: k*cos + (-k[d+D/2])*sin
-          kf[ks + KS / 2][e] = hi_v * c + lo_v * sn; // d >= D/2: k*cos + k[d-D/2]*sin
+          rl[e] = lo_f[e] * c - hi_f[e] * sn;  // d < D/2: k*cos + (-k[d+D/2])*sin
+          rh[e] = hi_f[e] * c + lo_f[e] * sn;  // d >= D/2: k*cos + k[d-D/2]*sin
         }
-      }
-      float acc[NT][4];
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) acc[nt][i] = 0.f;
-#pragma unroll
-      for (int ks = 0; ks < KS; ++ks) {
-        const uint32_t a[4] = {pack_f16(kf[ks][0], kf[ks][1]), pack_f16(kf[ks][2], kf[ks][3]),
-                               pack_f16(kf[ks][4], kf[ks][5]), pack_f16(kf[ks][6], kf[ks][7])};
+        const uint32_t al[4] = {pack_f16(rl[0], rl[1]), pack_f16(rl[2], rl[3]), pack_f16(rl[4], rl[5]),
+                                pack_f16(rl[6], rl[7])};
+        const uint32_t ah[4] = {pack_f16(rh[0], rh[1]), pack_f16(rh[2], rh[3]), pack_f16(rh[4], rh[5]),
+                                pack_f16(rh[6], rh[7])};
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-          mma16816(acc[nt], a, qh[nt][ks][0], qh[nt][ks][1]);
-          mma16816(acc[nt], a, ql[nt][ks][0], ql[nt][ks][1]);
+          mma16816(acc[nt], al, qh[nt][ks][0], qh[nt][ks][1]);
+          mma16816(acc[nt], al, ql[nt][ks][0], ql[nt][ks][1]);
+          mma16816(acc[nt], ah, qh[nt][ks + KS / 2][0], qh[nt][ks + KS / 2][1]);
+          mma16816(acc[nt], ah, ql[nt][ks + KS / 2][0], ql[nt][ks + KS / 2][1]);
+        }
+      };
+      if constexpr (MODE == BG_KV_F16) {
+#pragma unroll
+        for (int ks = 0; ks < KS / 2; ++ks) {
+          uint32_t a[4], a2[4];
+          ldsm_x4(a, swz<TP>(kb, row0 + lrow, 2 * ks + lhi));
+          ldsm_x4(a2, swz<TP>(kb, row0 + lrow, 2 * (ks + KS / 2) + lhi));
+          float lo_f[8], hi_f[8];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&a[i]));
+            const float2 g = __half22float2(*reinterpret_cast<const __half2 *>(&a2[i]));
+            lo_f[2 * i] = f.x;
+            lo_f[2 * i + 1] = f.y;
+            hi_f[2 * i] = g.x;
+            hi_f[2 * i + 1] = g.y;
+          }
+          rotate_mma(lo_f, hi_f, ks);
+        }
+      } else {
+        const float *ksc = reinterpret_cast<const float *>(smem + s * C::STAGE + 2 * C::KVT);
+        // snorm8 read: max(code/127, -1) * scale == max(code, -127) * (scale/127); the code is
+        // turned into an exact f16 by the 0x64XX trick (value 1152 + code) and unbiased in f16.
+        const __half2 bias = __half2(__float2half_rn(1152.f), __float2half_rn(1152.f));
+        const __half2 lo127 = __half2(__float2half_rn(-127.f), __float2half_rn(-127.f));
+        auto deq = [&](uint32_t w, uint32_t sel) {
+          const uint32_t hb = i8pair_biased(w ^ 0x80808080u, sel);
+          return __half22float2(__hmax2(__hsub2(*reinterpret_cast<const __half2 *>(&hb), bias), lo127));
+        };
+#pragma unroll
+        for (int bk = 0; bk < NB / 2; ++bk) {
+          uint32_t r[4], r2[4];
+          ldsm_x4(r, swz<TP>(kb, row0 + lrow, 2 * bk + lhi));
+          ldsm_x4(r2, swz<TP>(kb, row0 + lrow, 2 * (bk + NB / 2) + lhi));
+          const int ra = (row0 + (lane >> 2)) * NB;
+          const float s0 = ksc[ra + bk] * (1.0f / 127.0f), s1 = ksc[ra + 8 * NB + bk] * (1.0f / 127.0f);
+          const float t0 = ksc[ra + bk + NB / 2] * (1.0f / 127.0f),
+                      t1 = ksc[ra + 8 * NB + bk + NB / 2] * (1.0f / 127.0f);
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {  // k step 2bk + h2 from words r[2h2] (row a), r[2h2+1] (row b)
+            float lo_f[8], hi_f[8];
+            // a0 = bytes 0,1 of row a; a1 = bytes 0,1 of row b; a2 = bytes 2,3 of row a; a3 = row b
+            const float2 x0 = deq(r[2 * h2], kSelLo), x1 = deq(r[2 * h2 + 1], kSelLo);
+            const float2 x2 = deq(r[2 * h2], kSelHi), x3 = deq(r[2 * h2 + 1], kSelHi);
+            const float2 y0 = deq(r2[2 * h2], kSelLo), y1 = deq(r2[2 * h2 + 1], kSelLo);
+            const float2 y2 = deq(r2[2 * h2], kSelHi), y3 = deq(r2[2 * h2 + 1], kSelHi);
+            lo_f[0] = x0.x * s0; lo_f[1] = x0.y * s0; lo_f[2] = x1.x * s1; lo_f[3] = x1.y * s1;
+            lo_f[4] = x2.x * s0; lo_f[5] = x2.y * s0; lo_f[6] = x3.x * s1; lo_f[7] = x3.y * s1;
+            hi_f[0] = y0.x * t0; hi_f[1] = y0.y * t0; hi_f[2] = y1.x * t1; hi_f[3] = y1.y * t1;
+            hi_f[4] = y2.x * t0; hi_f[5] = y2.y * t0; hi_f[6] = y3.x * t1; hi_f[7] = y3.y * t1;
+            rotate_mma(lo_f, hi_f, 2 * bk + h2);
+          }
         }
       }
 #pragma unroll
