@@ -159,6 +159,7 @@ int bg_force_generic(int on) {
 int bg_device_status(bg_stream_t stream) {
   if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return BG_ELAUNCH;
   int e = poll_device_error_attn_tc();
+  if (!e) e = poll_device_error_attn_roll();
   if (!e) e = poll_device_error_prefill();
   return e ? (e < 0 ? e : BG_ELAUNCH) : BG_OK;
 }

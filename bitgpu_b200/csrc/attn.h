@@ -37,7 +37,15 @@ int launch_attn_tc(const AttnArgs &a, cudaStream_t st);  // returns BG_EUNSUPPOR
 int launch_lse_merge(const float *partials, uint32_t nsplit, uint32_t rows, uint32_t D,
                      const float *gate, void *out, int out_f16, cudaStream_t st);
 
+// Rope-at-read decode with all kv heads of a group per CTA (stream-K schedule); its split count
+// is fixed by the schedule, and launch_attn_roll returns BG_EUNSUPPORTED when a.nsplit differs.
+bool attn_roll_supported(int mode, uint32_t D, uint32_t S, uint32_t H, uint32_t KV);
+uint32_t attn_roll_num_splits(int mode, uint32_t B, uint32_t KV, uint32_t L);
+int launch_attn_roll(const AttnArgs &a, cudaStream_t st);
+bool roll_legacy();  // BGATTN_ROLL_LEGACY=1 selects the one-head-per-CTA kernel
+
 // Read-and-clear the bounded-wait timeout flag of the TMA kernels (BG_ETIMEOUT or 0).
 int poll_device_error_attn_tc();
+int poll_device_error_attn_roll();
 
 }  // namespace bg

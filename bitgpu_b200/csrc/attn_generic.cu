@@ -349,6 +349,7 @@ int attn_generic_ctas_per_sm(int mode, uint32_t D, uint32_t rows, bool roll) {
 // write + merge read.  Splits never get shorter than 256 positions.
 uint32_t attn_num_splits(uint32_t B, uint32_t S, uint32_t H, uint32_t KV, uint32_t D, uint32_t L, int mode, bool tc,
                          bool roll) {
+  if (tc && roll && attn_roll_supported(mode, D, S, H, KV) && !roll_legacy()) return attn_roll_num_splits(mode, B, KV, L);
   const uint32_t G = H / KV;
   const uint32_t M = S * G;
   const uint32_t rb = D >= 256 ? 4 : 8;

@@ -20,9 +20,11 @@
 // split partials [split][row][D+2] for the LSE merge kernel (shared with the generic path).
 #include <cuda.h>
 #include <cuda_fp16.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include "attn.h"
+#include "mma.cuh"
 #include "tma.cuh"
 
 // CTAs per SM the q8 rope-at-read kernel is compiled for (3: 128 registers, a few spills)
@@ -69,57 +71,6 @@ struct Cfg {
   static constexpr int NST = NST_RAW < 2 ? 2 : (NST_RAW > 6 ? 6 : NST_RAW);
   static constexpr int SMEM = NST * STAGE + 1024 /*align*/ + 2 * NST * 8 /*barriers*/ + 16 * NB * 4 /*q8 seeds*/;
 };
-
-__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(addr));
-}
-
-__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(addr));
-}
-
-__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ uint32_t movm_t(uint32_t x) {
-  uint32_t y;
-  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
-  return y;
-}
-
-__device__ __forceinline__ uint32_t pack_f16(float lo, float hi) {
-  __half2 h = __floats2half2_rn(lo, hi);
-  return *reinterpret_cast<uint32_t *>(&h);
-}
-
-constexpr uint32_t kSelLo = 0x4140, kSelHi = 0x4342, kSelEven = 0x4240, kSelOdd = 0x4341;
-
-// Biased form without the subtraction: (code + 1152) as exact f16x2, from a word already xored
-// with 0x80808080.  The kernels remove the +1152 inside the MMA instead (accumulator seed for K,
-// an extra MMA with a constant -1152 operand for V).
-__device__ __forceinline__ uint32_t i8pair_biased(uint32_t wx, uint32_t sel) {
-  return __byte_perm(wx, 0x64646464u, sel);
-}
-__device__ __forceinline__ uint32_t kNeg1152x2() {
-  __half2 h = __half2(__float2half_rn(-1152.f), __float2half_rn(-1152.f));
-  return *reinterpret_cast<uint32_t *>(&h);
-}
-
-// Shared-memory byte address of 16-byte chunk `gc` of tile row `row` (128B-swizzled column blocks
-// of TP rows each, the layout TMA writes with CU_TENSOR_MAP_SWIZZLE_128B).
-template <int TP>
-__device__ __forceinline__ uint32_t swz(uint32_t base, int row, int gc) {
-  return base + (gc >> 3) * (TP * 128) + row * 128 + (((gc & 7) ^ (row & 7)) << 4);
-}
 
 template <int MODE, int D, int NT, bool ROLL>
 __global__ void __launch_bounds__(160, (MODE == BG_KV_Q8 && NT == 1 && D == 128 && !ROLL) ? 3 : (ROLL && NT == 1 ? (MODE == BG_KV_Q8 ? BG_ROLL_Q8_MINB : 2) : 1)) attn_tc_kernel(
@@ -795,8 +746,20 @@ int attn_tc_ctas_per_sm(int mode, uint32_t D, uint32_t M, bool roll) {
   return M <= 8 ? occupancy<BG_KV_Q8, 128, 1>() : occupancy<BG_KV_Q8, 128, 2>();
 }
 
+bool roll_legacy() {
+  static const bool v = [] {
+    const char *e = getenv("BGATTN_ROLL_LEGACY");  // one-head-per-CTA rope-at-read kernel (A/B)
+    return e && *e == '1';
+  }();
+  return v;
+}
+
 int launch_attn_tc(const AttnArgs &a, cudaStream_t st) {
   if (!attn_tc_supported(a.mode, a.D, a.S, a.H, a.KV, a.cosT != nullptr, a.kv.window != 0)) return BG_EUNSUPPORTED;
+  if (a.cosT && !roll_legacy()) {
+    const int rc = launch_attn_roll(a, st);
+    if (rc != BG_EUNSUPPORTED) return rc;
+  }
   const uint32_t M = a.S * (a.H / a.KV);
   return a.mode == BG_KV_F16 ? launch_mode<BG_KV_F16>(a, M, st) : launch_mode<BG_KV_Q8>(a, M, st);
 }
