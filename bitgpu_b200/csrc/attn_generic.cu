@@ -247,6 +247,95 @@ __global__ void lse_merge_kernel(const float *__restrict__ part, uint32_t nsplit
   else static_cast<float *>(out)[(uint64_t)row * D + d] = o;
 }
 
+// Warp-parallel LSE merge: WPR warps per output row (WPR in {1,2,4,8}), warp k of a row takes
+// splits k, k + WPR, ... (at most kMergeSpw each, up to 64 splits).  Every warp loads its o values
+// first, then all (m, l) of the row (lane j: splits j, j+32), so a row costs one global round
+// trip; the WPR partial sums are combined through shared memory.
+constexpr int kMergeSpw = 8;
+
+template <int DPL>
+__global__ void __launch_bounds__(256) lse_merge_warp_kernel(const float *__restrict__ part, uint32_t nsplit,
+                                                             uint32_t rows, uint32_t wpr,
+                                                             const float *__restrict__ gate, void *out,
+                                                             int out_f16) {
+  constexpr uint32_t D = DPL * 32;
+  __shared__ float red[8][D];
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t row = blockIdx.x * (8 / wpr) + warp / wpr, k = warp % wpr;
+  const bool live = row < rows;
+  const uint64_t stride = (uint64_t)rows * (D + 2);
+  const float *base = part + (uint64_t)(live ? row : 0) * (D + 2);
+  float vals[kMergeSpw][DPL];
+#pragma unroll
+  for (int i = 0; i < kMergeSpw; ++i) {
+    const uint32_t sp = k + i * wpr;
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) vals[i][j] = (live && sp < nsplit) ? __ldg(base + sp * stride + lane + 32 * j) : 0.f;
+  }
+  float mv[2], lv[2];
+  float M = -INFINITY;
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    const uint32_t sp = lane + 32 * c;
+    mv[c] = -INFINITY;
+    lv[c] = 0.f;
+    if (live && sp < nsplit) {
+      lv[c] = __ldg(base + sp * stride + D + 1);
+      mv[c] = __ldg(base + sp * stride + D);
+      if (lv[c] > 0.f) M = fmaxf(M, mv[c]);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  float L = 0.f, f[2];
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    f[c] = lv[c] > 0.f ? expf(mv[c] - M) : 0.f;
+    L = fmaf(lv[c], f[c], L);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+  float acc[DPL];
+#pragma unroll
+  for (int j = 0; j < DPL; ++j) acc[j] = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMergeSpw; ++i) {
+    const uint32_t sp = k + i * wpr;  // warp-uniform
+    const float fs = __shfl_sync(0xffffffffu, sp < 32 ? f[0] : f[1], sp & 31);
+    const bool use = sp < nsplit && fs != 0.f;  // empty slots may hold any bits
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) acc[j] = use ? fmaf(vals[i][j], fs, acc[j]) : acc[j];
+  }
+  if (wpr > 1) {
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) red[warp][lane + 32 * j] = acc[j];
+    __syncthreads();
+    if (k != 0) return;
+    for (uint32_t w = 1; w < wpr; ++w)
+#pragma unroll
+      for (int j = 0; j < DPL; ++j) acc[j] += red[warp + w][lane + 32 * j];
+  }
+  if (!live) return;
+  if (out_f16 < 0) {
+    float *dst = static_cast<float *>(out) + (uint64_t)row * (D + 2);
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) dst[lane + 32 * j] = acc[j];
+    if (lane == 0) {
+      dst[D] = L > 0.f ? M : -INFINITY;
+      dst[D + 1] = L;
+    }
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < DPL; ++j) {
+    const uint32_t d = lane + 32 * j;
+    float o = acc[j] / L;
+    if (gate) o = o / (1.0f + expf(-gate[(uint64_t)row * D + d]));
+    if (out_f16) static_cast<__half *>(out)[(uint64_t)row * D + d] = __float2half_rn(o);
+    else static_cast<float *>(out)[(uint64_t)row * D + d] = o;
+  }
+}
+
 template <int MODE, int D, bool ROLL>
 int launch_rb(const AttnArgs &a, cudaStream_t st) {
   const uint32_t rows = a.S * (a.H / a.KV);
@@ -408,6 +497,15 @@ int launch_lse_merge(const float *partials, uint32_t nsplit, uint32_t rows, uint
                      const float *gate, void *out, int out_f16, cudaStream_t st) {
   if (rows == 0) return BG_OK;
   if (D > 1024) return BG_EUNSUPPORTED;
+  if (nsplit <= 8 * kMergeSpw && (D == 64 || D == 128 || D == 256)) {
+    uint32_t wpr = 1;
+    while (wpr * kMergeSpw < nsplit) wpr *= 2;
+    const uint32_t rpb = 8 / wpr, blocks = (rows + rpb - 1) / rpb;
+    if (D == 64) lse_merge_warp_kernel<2><<<blocks, 256, 0, st>>>(partials, nsplit, rows, wpr, gate, out, out_f16);
+    else if (D == 128) lse_merge_warp_kernel<4><<<blocks, 256, 0, st>>>(partials, nsplit, rows, wpr, gate, out, out_f16);
+    else lse_merge_warp_kernel<8><<<blocks, 256, 0, st>>>(partials, nsplit, rows, wpr, gate, out, out_f16);
+    return cudaGetLastError() == cudaSuccess ? BG_OK : BG_ELAUNCH;
+  }
   // as many split groups as fit 1024 threads, but no more than there are splits
   uint32_t groups = 1024 / D;
   if (groups > nsplit) groups = nsplit;

@@ -35,6 +35,12 @@
 #include "mma.cuh"
 #include "tma.cuh"
 
+// 1: rotate in packed f16 (fewer issue slots; errors ~2x the f32 form, far inside tolerance);
+// 0: rotate in f32 and round once to f16.
+#ifndef BG_ROLL_ROT_F16
+#define BG_ROLL_ROT_F16 1
+#endif
+
 namespace bg {
 namespace {
 
@@ -279,7 +285,112 @@ __global__ void __launch_bounds__(RCfg<MODE, HPC>::THREADS, 1)
       const bool va_ok = (uint32_t)ra < tl.n, vb_ok = (uint32_t)(ra + 8) < tl.n;
 
       // ---- scores S^T = rot(K) . Q^T, one pair of k steps (dims d, d + D/2) at a time ----
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      // four independent accumulators (one per pair of k steps) keep the MMA chains short
+      float acc4[KS / 2][4];
+#pragma unroll
+      for (int c = 0; c < KS / 2; ++c)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc4[c][i] = 0.f;
+#if BG_ROLL_ROT_F16
+      // Packed-f16 rotation: register slot i of an A fragment holds two consecutive dims of row a
+      // (i even) or b (i odd); its partner slot in step ks + KS/2 holds the same dims + D/2.
+      // cos/sin are read as f32 from the staged slice and packed once per row and slot.
+      auto rotate_mma = [&](const uint32_t (&kl)[4], const uint32_t (&kh)[4], int ks) {
+        __half2 cs[4], sn[4], nsn[4];
+#pragma unroll
+        for (int rb = 0; rb < 2; ++rb) {
+          const int r = ra + 8 * rb;
+          if constexpr (MODE == BG_KV_F16) {
+            const int c = ks * 4 + ((lane & 3) >> 1);  // dims d0 = ks*16 + 2*(lane&3) and d0 + 8
+            const uint32_t o0 = (r * 16 + (c ^ (r & 7))) * 16 + 8 * (lane & 1);
+            const uint32_t o1 = (r * 16 + ((c + 2) ^ (r & 7))) * 16 + 8 * (lane & 1);
+            float2 c0, c1, s0, s1;
+            asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(c0.x), "=f"(c0.y) : "r"(tcos + o0));
+            asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(c1.x), "=f"(c1.y) : "r"(tcos + o1));
+            asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(s0.x), "=f"(s0.y) : "r"(tsin + o0));
+            asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(s1.x), "=f"(s1.y) : "r"(tsin + o1));
+            cs[rb] = __float22half2_rn(c0);
+            cs[2 + rb] = __float22half2_rn(c1);
+            sn[rb] = __float22half2_rn(s0);
+            sn[2 + rb] = __float22half2_rn(s1);
+          } else {
+            const int c = (ks >> 1) * 8 + (ks & 1) * 4 + (lane & 3);  // dims 4c .. 4c+3
+            const uint32_t o = (r * 16 + (c ^ (r & 7))) * 16;
+            float4 c4, s4;
+            asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+                         : "=f"(c4.x), "=f"(c4.y), "=f"(c4.z), "=f"(c4.w)
+                         : "r"(tcos + o));
+            asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+                         : "=f"(s4.x), "=f"(s4.y), "=f"(s4.z), "=f"(s4.w)
+                         : "r"(tsin + o));
+            cs[rb] = __floats2half2_rn(c4.x, c4.y);
+            cs[2 + rb] = __floats2half2_rn(c4.z, c4.w);
+            sn[rb] = __floats2half2_rn(s4.x, s4.y);
+            sn[2 + rb] = __floats2half2_rn(s4.z, s4.w);
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) nsn[i] = __hneg2(sn[i]);
+        uint32_t al[4], ah[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const __half2 lo_h = *reinterpret_cast<const __half2 *>(&kl[i]);
+          const __half2 hi_h = *reinterpret_cast<const __half2 *>(&kh[i]);
+          const __half2 rl = __hfma2(hi_h, nsn[i], __hmul2(lo_h, cs[i]));  // k*cos - k[d+D/2]*sin
+          const __half2 rh = __hfma2(lo_h, sn[i], __hmul2(hi_h, cs[i]));   // k*cos + k[d-D/2]*sin
+          al[i] = *reinterpret_cast<const uint32_t *>(&rl);
+          ah[i] = *reinterpret_cast<const uint32_t *>(&rh);
+        }
+        float (&acc)[4] = acc4[ks];
+        mma16816(acc, al, qh[ks][0], qh[ks][1]);
+        mma16816(acc, ah, qh[ks + KS / 2][0], qh[ks + KS / 2][1]);
+        mma16816(acc, al, ql[ks][0], ql[ks][1]);
+        mma16816(acc, ah, ql[ks + KS / 2][0], ql[ks + KS / 2][1]);
+      };
+      if constexpr (MODE == BG_KV_F16) {
+#pragma unroll
+        for (int ks = 0; ks < KS / 2; ++ks) {
+          uint32_t a[4], a2[4];
+          ldsm_x4(a, swz<ROWS>(kb, row0 + lrow, 2 * ks + lhi));
+          ldsm_x4(a2, swz<ROWS>(kb, row0 + lrow, 2 * (ks + KS / 2) + lhi));
+          rotate_mma(a, a2, ks);
+        }
+      } else {
+        // snorm8 read: max(code, -127) * (scale/127): the code becomes the exact f16 1152 + code
+        // (0x64XX), is clamped and unbiased exactly in f16, then scaled by scale/127 in f16
+        const __half2 bias = __float2half2_rn(1152.f), lo127 = __float2half2_rn(1025.f);
+        auto deq = [&](uint32_t wx, uint32_t sel, __half2 sc) {
+          const uint32_t hb = i8pair_biased(wx, sel);
+          const __half2 v = __hmul2(__hsub2(__hmax2(*reinterpret_cast<const __half2 *>(&hb), lo127), bias), sc);
+          return *reinterpret_cast<const uint32_t *>(&v);
+        };
+        const int sa_i = (ra * HPC + warp) * NB, sb_i = ((ra + 8) * HPC + warp) * NB;
+#pragma unroll
+        for (int bk = 0; bk < NB / 2; ++bk) {
+          uint32_t r[4], r2[4];
+          ldsm_x4(r, swz<ROWS>(kb, row0 + lrow, 2 * bk + lhi));
+          ldsm_x4(r2, swz<ROWS>(kb, row0 + lrow, 2 * (bk + NB / 2) + lhi));
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            r[i] ^= 0x80808080u;
+            r2[i] ^= 0x80808080u;
+          }
+          const __half2 s0 = __float2half2_rn(ksc[sa_i + bk] * (1.0f / 127.0f));
+          const __half2 s1 = __float2half2_rn(ksc[sb_i + bk] * (1.0f / 127.0f));
+          const __half2 t0 = __float2half2_rn(ksc[sa_i + bk + NB / 2] * (1.0f / 127.0f));
+          const __half2 t1 = __float2half2_rn(ksc[sb_i + bk + NB / 2] * (1.0f / 127.0f));
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {  // k step 2bk + h2 from words r[2h2] (row a), r[2h2+1] (row b)
+            // a0 = bytes 0,1 of row a; a1 = bytes 0,1 of row b; a2 = bytes 2,3 of row a; a3 = row b
+            const uint32_t kl[4] = {deq(r[2 * h2], kSelLo, s0), deq(r[2 * h2 + 1], kSelLo, s1),
+                                    deq(r[2 * h2], kSelHi, s0), deq(r[2 * h2 + 1], kSelHi, s1)};
+            const uint32_t kh[4] = {deq(r2[2 * h2], kSelLo, t0), deq(r2[2 * h2 + 1], kSelLo, t1),
+                                    deq(r2[2 * h2], kSelHi, t0), deq(r2[2 * h2 + 1], kSelHi, t1)};
+            rotate_mma(kl, kh, 2 * bk + h2);
+          }
+        }
+      }
+#else
       auto rotate_mma = [&](float (&lo_f)[8], float (&hi_f)[8], int ks) {
         float cr_[2][4], sr_[2][4];  // [row a/b][dim slot]
 #pragma unroll
@@ -324,9 +435,10 @@ __global__ void __launch_bounds__(RCfg<MODE, HPC>::THREADS, 1)
                                 pack_f16(rl[6], rl[7])};
         const uint32_t ah[4] = {pack_f16(rh[0], rh[1]), pack_f16(rh[2], rh[3]), pack_f16(rh[4], rh[5]),
                                 pack_f16(rh[6], rh[7])};
+        float (&acc)[4] = acc4[ks];
         mma16816(acc, al, qh[ks][0], qh[ks][1]);
-        mma16816(acc, al, ql[ks][0], ql[ks][1]);
         mma16816(acc, ah, qh[ks + KS / 2][0], qh[ks + KS / 2][1]);
+        mma16816(acc, al, ql[ks][0], ql[ks][1]);
         mma16816(acc, ah, ql[ks + KS / 2][0], ql[ks + KS / 2][1]);
       };
       if constexpr (MODE == BG_KV_F16) {
@@ -373,6 +485,11 @@ __global__ void __launch_bounds__(RCfg<MODE, HPC>::THREADS, 1)
           }
         }
       }
+
+#endif
+      float acc[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[i] = (acc4[0][i] + acc4[1][i]) + (acc4[2][i] + acc4[3][i]);
 
       // ---- online softmax (columns n0 = 2(lane%4), n1 = n0+1; rows pa, pb) ----
       float pr[4], cr[2];

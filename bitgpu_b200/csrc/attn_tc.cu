@@ -426,11 +426,13 @@ __global__ void __launch_bounds__(160, (MODE == BG_KV_Q8 && NT == 1 && D == 128 
 #pragma unroll
         for (int i = 0; i < 4; ++i) sc[nt][i] = acc[nt][i] * p.sl2;
     } else if constexpr (MODE == BG_KV_F16) {
-      float acc[NT][4];
+      // hi and lo halves of Q accumulate into separate chains (D = 256 would otherwise chain
+      // 32 dependent MMAs per tile)
+      float acc[NT][4], acl[NT][4];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) acc[nt][i] = 0.f;
+        for (int i = 0; i < 4; ++i) acc[nt][i] = acl[nt][i] = 0.f;
 #pragma unroll
       for (int ks = 0; ks < KS; ++ks) {
         uint32_t a[4];
@@ -438,13 +440,13 @@ __global__ void __launch_bounds__(160, (MODE == BG_KV_Q8 && NT == 1 && D == 128 
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
           mma16816(acc[nt], a, qh[nt][ks][0], qh[nt][ks][1]);
-          mma16816(acc[nt], a, ql[nt][ks][0], ql[nt][ks][1]);
+          mma16816(acl[nt], a, ql[nt][ks][0], ql[nt][ks][1]);
         }
       }
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) sc[nt][i] = acc[nt][i] * p.sl2;
+        for (int i = 0; i < 4; ++i) sc[nt][i] = (acc[nt][i] + acl[nt][i]) * p.sl2;
     } else {
       const float *ksc = reinterpret_cast<const float *>(smem + s * C::STAGE + 2 * C::KVT);
       float acc[NT][NB][4];

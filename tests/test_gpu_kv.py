@@ -99,7 +99,12 @@ def test_evict_compaction_matches_engine(ops, mode):
 
 
 def test_ring_equals_compaction(ops):
-    """Attention over a ring cache after ring evictions == over a compacted linear cache."""
+    """Attention over a ring cache after ring evictions == over a compacted linear cache.
+
+    Both caches hold the same bytes per logical slot; the rope-at-read kernel cuts its tiles at
+    the ring's physical discontinuities, so the two summation orders (and the f16 rounding of the
+    softmax weights against different running maxima) may differ at the kernel's rounding level,
+    ~1e-4; a layout error would show as O(0.1)."""
     rng = np.random.default_rng(13)
     B, H, KV, D, SINKS, MAX = 2, 16, 8, 128, 4, 132
     c, s = OR.synth_rope(D, MAX, 1e6, "yarn", 4.0, 8192)
@@ -122,7 +127,8 @@ def test_ring_equals_compaction(ops):
             q = torch.from_numpy(rand(rng, B, 1, H, D)).cuda()
             a = ops.attention(q, ring, fill - 1, cos_t=cos_t, sin_t=sin_t)
             b = ops.attention(q, lin, fill - 1, cos_t=cos_t, sin_t=sin_t)
-            assert torch.equal(a, b), step
+            err = (a - b).abs().max().item()
+            assert err <= 5e-4, (step, err)
     assert ring.ring_head != 0
 
 
