@@ -414,8 +414,7 @@ def run_roll(torch, ops, args, rank, barrier, max_over_ranks):
     def step():
         t = state["t"] % T
         f = cache.evict_for(state["fill"], 1, maxlen)
-        cache.append(0, ks[t], f)
-        cache.append(1, vs[t], f)
+        cache.append_kv(ks[t], vs[t], f)
         ops.attention(qs[t], cache, f, cos_t=cos_t, sin_t=sin_t, out=out)
         state["fill"] = f + 1
         state["t"] += 1
@@ -519,8 +518,8 @@ def run_ours(args):
                           {"workload": f"config 4: H16 KV8 D128, batch {args.roll_batch}, 4 sinks + 4096 ring, "
                                        f"{r['steps']} consecutive decode steps from fill 3076 (crossing "
                                        f"evictions)", "l2": "cache ~150 MB >> L2 only partly"},
-                          hbm_roof(r["gbs"], "mean algorithmic bytes per step / mean step time (append x2 + "
-                                             "attention)"), 3 * r["steps"], clk.stop())
+                          hbm_roof(r["gbs"], "mean algorithmic bytes per step / mean step time (fused K+V "
+                                             "append, attention, LSE merge)"), 3 * r["steps"], clk.stop())
         line["steps"] = r["steps"]
         return finish(line)
 
@@ -556,8 +555,7 @@ def run_ours(args):
                 qd.copy_(qh, non_blocking=True)
                 kd.copy_(kh, non_blocking=True)
                 vd.copy_(vh, non_blocking=True)
-                cache.append(0, kd, L - 1)
-                cache.append(1, vd, L - 1)
+                cache.append_kv(kd, vd, L - 1)
                 ops.attention(qd, cache, L - 1, out=out)
                 oh.copy_(out, non_blocking=True)
                 torch.cuda.current_stream().synchronize()
@@ -566,7 +564,7 @@ def run_ours(args):
             res["e2e"] = {"value": round(ab * ws / (ms_e2e * 1e-3) / 1e9, 2), "unit": "GB/s",
                           "h2d_bytes_per_step": (qh.numel() + kh.numel() + vh.numel()) * 4,
                           "d2h_bytes_per_step": oh.numel() * 4, "ms_per_step": round(ms_e2e, 4),
-                          "path": "bitgpu_b200.ops (ctypes -> libbgattn.so C ABI): bg_kv_append x2 + bg_attention"}
+                          "path": "bitgpu_b200.ops (ctypes -> libbgattn.so C ABI): bg_kv_append_kv + bg_attention"}
         results[mode] = res
         del cache
         torch.cuda.empty_cache()

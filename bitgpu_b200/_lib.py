@@ -16,7 +16,7 @@ DT_F32, DT_F16 = 0, 1
 # every symbol include/bgattn.h declares (checked by the CPU test suite)
 EXPORTS = [
     "bg_strerror", "bg_version", "bg_device_status", "bg_force_generic", "bg_attention_workspace_size", "bg_attention", "bg_attention_partials",
-    "bg_lse_merge", "bg_kv_append", "bg_rmsnorm_rope", "bg_kv_evict", "bg_kv_ring_evict",
+    "bg_lse_merge", "bg_kv_append", "bg_kv_append_kv", "bg_rmsnorm_rope", "bg_kv_evict", "bg_kv_ring_evict",
     "bg_deltanet_gbeta", "bg_deltanet_recur", "bg_deltanet_norm_gate", "bg_deltanet_fused",
     "bg_gate_sigmoid", "bg_attention_noalloc", "bg_deltanet_chunked_workspace_size",
     "bg_deltanet_chunked",
@@ -55,6 +55,7 @@ _SIGS = {
                                         U32, P, P, SZ, P]),
     "bg_lse_merge": (C.c_int, [P, U32, U32, U32, P, P, U32, P]),
     "bg_kv_append": (C.c_int, [C.POINTER(KVCacheDesc), U32, U32, P, U32, U32, U32, U32, U32, P]),
+    "bg_kv_append_kv": (C.c_int, [C.POINTER(KVCacheDesc), U32, P, P, U32, U32, U32, U32, U32, P]),
     "bg_rmsnorm_rope": (C.c_int, [P, U32, U32, U32, P, P, P, F, P, C.POINTER(KVCacheDesc), U32, P]),
     "bg_kv_evict": (C.c_int, [C.POINTER(KVCacheDesc), U32, U32, U32, U32, U32, U32, C.POINTER(U32), P]),
     "bg_kv_ring_evict": (C.c_int, [C.POINTER(KVCacheDesc), U32, U32, U32, C.POINTER(U32)]),

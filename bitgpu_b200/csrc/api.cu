@@ -220,8 +220,22 @@ int bg_kv_append(const bg_kv_cache *kv, uint32_t which, uint32_t batch, const vo
   const uint64_t cap = kv->window ? (uint64_t)kv->sinks + kv->window : kv->seq_stride;
   if ((uint64_t)pos0 + S > cap) return BG_EINVAL;  // the engine's ensureKvCapacity / evictFor precondition
   if (batch == 0 || S == 0) return BG_OK;
-  return launch_kv_append(make_view(kv, KV, 0), (int)kv->mode, D, src, src_dtype == BG_DT_F16, batch, S, pos0,
-                          (int)which, (cudaStream_t)stream);
+  return launch_kv_append(make_view(kv, KV, 0), (int)kv->mode, D, src, nullptr, src_dtype == BG_DT_F16, batch, S,
+                          pos0, (int)which, 1, (cudaStream_t)stream);
+}
+
+int bg_kv_append_kv(const bg_kv_cache *kv, uint32_t batch, const void *k_src, const void *v_src, uint32_t src_dtype,
+                    uint32_t S, uint32_t KV, uint32_t D, uint32_t pos0, bg_stream_t stream) {
+  if (!kv || !k_src || !v_src || src_dtype > BG_DT_F16 || !kv_mode_ok(kv->mode) || KV == 0) return BG_EINVAL;
+  if (!d_ok(D)) return BG_EUNSUPPORTED;
+  if (kv->mode == BG_KV_Q8R && D % 128) return BG_EINVAL;
+  if (!kv->K || !kv->V) return BG_EINVAL;
+  if ((kv->mode == BG_KV_Q8 || kv->mode == BG_KV_Q8R) && (!kv->Ks || !kv->Vs)) return BG_EINVAL;
+  const uint64_t cap = kv->window ? (uint64_t)kv->sinks + kv->window : kv->seq_stride;
+  if ((uint64_t)pos0 + S > cap) return BG_EINVAL;
+  if (batch == 0 || S == 0) return BG_OK;
+  return launch_kv_append(make_view(kv, KV, 0), (int)kv->mode, D, k_src, v_src, src_dtype == BG_DT_F16, batch, S,
+                          pos0, 0, 2, (cudaStream_t)stream);
 }
 
 int bg_rmsnorm_rope(const float *x, uint32_t batch, uint32_t R, uint32_t D, const float *gamma, const float *cos,

@@ -61,20 +61,25 @@ __device__ __forceinline__ void store_row(void *data, float *scales, int mode, u
   }
 }
 
+// Rows [side][b][s][kv]: side 0 writes src0 into the cache's `first_v ? V : K`, side 1 (when
+// nsides == 2) writes src1 into V.
 template <int DPL>
-__global__ void kv_append_kernel(KVView kv, int mode, const void *src, int src_f16, uint32_t B, uint32_t S,
-                                 uint32_t pos0, int which_v) {
+__global__ void kv_append_kernel(KVView kv, int mode, const void *src0, const void *src1, int src_f16, uint32_t B,
+                                 uint32_t S, uint32_t pos0, int first_v, int nsides) {
   constexpr int D = DPL * 32;
   const uint32_t gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t total = B * S * kv.KV;
-  if (gw >= total) return;
-  const uint32_t kvh = gw % kv.KV, s = (gw / kv.KV) % S, b = gw / (kv.KV * S);
+  if (gw >= total * nsides) return;
+  const int side = gw >= total;
+  const uint32_t r = gw - side * total;
+  const uint32_t kvh = r % kv.KV, s = (r / kv.KV) % S, b = r / (kv.KV * S);
+  const bool to_v = side || first_v;
   float x[DPL];
-  load_src<DPL>(src, src_f16, (uint64_t)gw * D + lane * DPL, x);
+  load_src<DPL>(side ? src1 : src0, src_f16, (uint64_t)r * D + lane * DPL, x);
   const uint64_t row = cache_row(kv, b, pos0 + s, kvh);
-  store_row<DPL>(const_cast<void *>(which_v ? kv.V : kv.K), const_cast<float *>(which_v ? kv.Vs : kv.Ks), mode,
-                 row, lane, x);
+  store_row<DPL>(const_cast<void *>(to_v ? kv.V : kv.K), const_cast<float *>(to_v ? kv.Vs : kv.Ks), mode, row, lane,
+                 x);
 }
 
 // rmsnorm_rope_sg.wgsl:21-33 (+ the _kv8 write side): y = (x*inv*gamma) rotated by cos/sin.
@@ -137,22 +142,22 @@ __global__ void copy_rows_kernel(uint8_t *base, uint64_t seq_bytes, uint64_t dst
 }
 
 template <int DPL>
-int launch_append_d(const KVView &kv, int mode, const void *src, int f16, uint32_t B, uint32_t S, uint32_t pos0,
-                    int which_v, cudaStream_t st) {
-  const uint64_t warps = (uint64_t)B * S * kv.KV;
+int launch_append_d(const KVView &kv, int mode, const void *src0, const void *src1, int f16, uint32_t B, uint32_t S,
+                    uint32_t pos0, int first_v, int nsides, cudaStream_t st) {
+  const uint64_t warps = (uint64_t)B * S * kv.KV * nsides;
   const uint32_t blocks = (uint32_t)((warps * 32 + 255) / 256);
-  kv_append_kernel<DPL><<<blocks, 256, 0, st>>>(kv, mode, src, f16, B, S, pos0, which_v);
+  kv_append_kernel<DPL><<<blocks, 256, 0, st>>>(kv, mode, src0, src1, f16, B, S, pos0, first_v, nsides);
   return cudaGetLastError() == cudaSuccess ? BG_OK : BG_ELAUNCH;
 }
 
 }  // namespace
 
-int launch_kv_append(const KVView &kv, int mode, uint32_t D, const void *src, int src_f16, uint32_t B, uint32_t S,
-                     uint32_t pos0, int which_v, cudaStream_t st) {
+int launch_kv_append(const KVView &kv, int mode, uint32_t D, const void *src0, const void *src1, int src_f16,
+                     uint32_t B, uint32_t S, uint32_t pos0, int first_v, int nsides, cudaStream_t st) {
   switch (D) {
-    case 64: return launch_append_d<2>(kv, mode, src, src_f16, B, S, pos0, which_v, st);
-    case 128: return launch_append_d<4>(kv, mode, src, src_f16, B, S, pos0, which_v, st);
-    case 256: return launch_append_d<8>(kv, mode, src, src_f16, B, S, pos0, which_v, st);
+    case 64: return launch_append_d<2>(kv, mode, src0, src1, src_f16, B, S, pos0, first_v, nsides, st);
+    case 128: return launch_append_d<4>(kv, mode, src0, src1, src_f16, B, S, pos0, first_v, nsides, st);
+    case 256: return launch_append_d<8>(kv, mode, src0, src1, src_f16, B, S, pos0, first_v, nsides, st);
     default: return BG_EUNSUPPORTED;
   }
 }

@@ -97,6 +97,17 @@ class KVCache:
         check("bg_kv_append", lib().bg_kv_append(C.byref(d), which, B, _p(src), _DT[src.dtype], S, KV, D, pos0,
                                                   _stream()))
 
+    def append_kv(self, k, v, pos0):
+        """Both writes of ``appendKV`` (K then V, same shapes and dtype) in one launch."""
+        _need(k, name="k")
+        _need(v, k.dtype, "v")
+        if k.shape != v.shape:
+            raise ValueError("k and v shapes differ")
+        B, S, KV, D = k.shape
+        d = self.desc()
+        check("bg_kv_append_kv", lib().bg_kv_append_kv(C.byref(d), B, _p(k), _p(v), _DT[k.dtype], S, KV, D, pos0,
+                                                        _stream()))
+
     def write_normed_k(self, x, gamma, eps, pos, cos=None, sin=None, y=None):
         """Fused K path of the decode step (``rmsnorm_rope_sg{,_kv16,_kv8}``, engine.ts:1533-1540):
         ``x[batch, KV, D]`` -> RMSNorm*gamma -> RoPE(cos, sin of this position; None = unroped)

@@ -125,6 +125,13 @@ int bg_kv_append(const bg_kv_cache *kv, uint32_t which, uint32_t batch, const vo
                  uint32_t src_dtype, uint32_t S, uint32_t KV, uint32_t D, uint32_t pos0,
                  bg_stream_t stream);
 
+/* bg_kv_append_kv: both writes of one appendKV step (engine.ts:1385-1393 dispatches the K and
+ * the V copy back to back) in a single launch; same layout, codec and errors as two
+ * bg_kv_append calls with which = 0 and 1. */
+int bg_kv_append_kv(const bg_kv_cache *kv, uint32_t batch, const void *k_src, const void *v_src,
+                    uint32_t src_dtype, uint32_t S, uint32_t KV, uint32_t D, uint32_t pos0,
+                    bg_stream_t stream);
+
 /* bg_rmsnorm_rope: rmsnorm_rope_sg{,_kv16,_kv8}.wgsl (engine.ts:1529-1540): per head row
  * y = rmsnorm(x)*gamma rotated by (cos, sin) ([D] tables of this position; NULL/NULL = no
  * rotation, the sink-mode cos=1/sin=0 binding of engine.ts:1533).  x [batch][R][D]; the result
