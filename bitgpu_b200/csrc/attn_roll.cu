@@ -16,8 +16,8 @@
 //     16 rows x HPC heads x 128 bytes, laid out head-major ([head][slot][128B], 128-byte swizzle)
 //     through a tensor map whose kv-head and slot strides are swapped; rows of a short tile past
 //     its segment are masked;
-//   * the producer warp issues the K/V TMA boxes (lane 0, expect_tx) and cp.async copies of the
-//     q8 block scales and of the two table slices (all lanes, arrive.noinc), into an NST-deep
+//   * three producer warps share the loads of a stage: the K/V TMA boxes (lane 0, expect_tx),
+//     the two table slices and the q8 block scales (cp.async, arrive.noinc), into an NST-deep
 //     mbarrier ring;
 //   * the grid is 148 x (resident CTAs per SM); CTA c processes flattened positions
 //     [c*W, (c+1)*W) of units x L, so every SM streams the same number of cache rows.  A unit
@@ -25,21 +25,19 @@
 //     the unit's first piece marks the unused partial slots empty, and the LSE merge kernel
 //     combines them.  When whole units fit per CTA the kernel writes the final rows itself.
 // Scores and outputs are computed transposed (S^T = K Q^T, O^T = V^T P^T, m16n8k16) exactly as in
-// the plain decode kernel; the rotation runs in f32 on the dequantised K fragment and the rotated
-// values are rounded once to f16 for the MMA, with Q split hi + lo.
+// the plain decode kernel, with Q split hi + lo.  K is dequantised and rotated in packed f16 (the
+// operand precision of the MMA; an f32 rotation rounded once was measured ~5% slower at half the
+// error, both far inside the 2e-3 gate).  Each consumer step takes two tiles when the piece has
+// them, so one max reduction covers 32 slots.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <string.h>
 
+#include <type_traits>
+
 #include "attn.h"
 #include "mma.cuh"
 #include "tma.cuh"
-
-// 1: rotate in packed f16 (fewer issue slots; errors ~2x the f32 form, far inside tolerance);
-// 0: rotate in f32 and round once to f16.
-#ifndef BG_ROLL_ROT_F16
-#define BG_ROLL_ROT_F16 1
-#endif
 
 namespace bg {
 namespace {
@@ -79,9 +77,24 @@ struct RCfg {
   static constexpr int STAGE = 2 * KVT + 2 * SCT + 2 * TBL;
   static constexpr int NST_RAW = (220 * 1024) / STAGE;
   static constexpr int NST = NST_RAW < 2 ? 2 : (NST_RAW > 8 ? 8 : NST_RAW);
-  static constexpr int THREADS = (HPC + 1) * 32;
+  // consumer warps fill whole warpgroups; warp CW of the warpgroup after them is the producer
+  static constexpr int CW = HPC < 4 ? 4 : HPC;
+  static constexpr int THREADS = (CW + 4) * 32;
+  // 384 threads launch at 168 registers (3 warps on some SM sub-partition); the producer
+  // warpgroup gives back to 40 and the two consumer warpgroups take 232: 128*40 + 256*232 ==
+  // 384*168.  Up to 256 threads need no split (255 registers each).
+  static constexpr bool SPLIT_REGS = THREADS > 256;
   static constexpr int SMEM = NST * STAGE + 1024 + 2 * NST * 8;
 };
+
+// XOR swizzle of the 16-byte chunks of a staged cos/sin row r.  q8 consumers read 16 bytes per
+// lane (one wavefront per quarter warp: rows 2i and 2i+1, four chunks each), f16 consumers 8 bytes
+// per lane (one wavefront per half warp: rows 4i..4i+3, two chunks each); these XORs put every
+// lane of a wavefront on a distinct 16-byte bank group.
+template <int MODE>
+__device__ __forceinline__ int tbl_swz(int r) {
+  return MODE == BG_KV_F16 ? ((r & 3) << 1) : ((r & 1) << 2);
+}
 
 struct Tile {
   uint32_t ph;  // physical row of the tile's first slot
@@ -141,16 +154,24 @@ __global__ void __launch_bounds__(RCfg<MODE, HPC>::THREADS, 1)
 
   if (tid == 0) {
     for (int s = 0; s < NST; ++s) {
-      mbar_init(&full[s], 33);  // lane 0's expect_tx arrival + 32 cp.async arrivals
+      // lane 0's expect_tx arrival + 32 cp.async arrivals per cp.async role (tables; q8 scales)
+      mbar_init(&full[s], MODE == BG_KV_Q8 ? 65 : 33);
       mbar_init(&empty[s], HPC);
     }
     fence_barrier_init();
   }
   __syncthreads();
   if (f0 >= f1) return;
+  static_assert(!C::SPLIT_REGS || C::THREADS == 384, "register split sized for 384 threads");
 
-  if (warp == HPC) {  // ---------------- producer warp ----------------
-    if (lane == 0) {
+  if (warp >= C::CW) {  // ---------------- producer warpgroup ----------------
+    // role 0: K/V boxes by TMA (lane 0, expect_tx); role 1: cos/sin slices by cp.async; role 2
+    // (q8): block scales by cp.async.  Each role walks the same tile sequence and waits for the
+    // stage to be released on its own; the cp.async roles arrive with noinc (32 arrivals each).
+    if constexpr (C::SPLIT_REGS) asm volatile("setmaxnreg.dec.sync.aligned.u32 40;" ::: "memory");
+    const int role = warp - C::CW;
+    if (role > (MODE == BG_KV_Q8 ? 2 : 1)) return;
+    if (role == 0 && lane == 0) {
       prefetch_tmap(&tmK);
       prefetch_tmap(&tmV);
     }
@@ -165,54 +186,73 @@ __global__ void __launch_bounds__(RCfg<MODE, HPC>::THREADS, 1)
         if (t >= NST) ok = mbar_wait_warp(&empty[s], ((t / NST) - 1) & 1);
         if (!ok) break;
         unsigned char *st = smem + s * C::STAGE;
-        if (lane == 0) {
-          mbar_expect_tx(&full[s], 2 * C::KVT);
-#pragma unroll
-          for (int cb = 0; cb < C::NCB; ++cb) {
-            tma_load_4d(st + cb * ROWS * 128, &tmK, &full[s], cb * (128 / C::ES), (int)tl.ph, (int)kv0, (int)b);
-            tma_load_4d(st + C::KVT + cb * ROWS * 128, &tmV, &full[s], cb * (128 / C::ES), (int)tl.ph, (int)kv0,
-                        (int)b);
-          }
-        }
         const uint32_t sbase = smem_u32(st + 2 * C::KVT);
-        if constexpr (MODE == BG_KV_Q8) {
-          // block scales [slot][head][NB] of both caches; slots past the tile are zero-filled
-          for (int idx = lane; idx < 2 * TP * HPC; idx += 32) {
-            const int which = idx / (TP * HPC), rem = idx % (TP * HPC);
-            const int r = rem / HPC, hh = rem % HPC;
+        if (role == 0) {
+          if (lane == 0) {
+            mbar_expect_tx(&full[s], 2 * C::KVT);
+#pragma unroll
+            for (int cb = 0; cb < C::NCB; ++cb) {
+              tma_load_4d(st + cb * ROWS * 128, &tmK, &full[s], cb * (128 / C::ES), (int)tl.ph, (int)kv0, (int)b);
+              tma_load_4d(st + C::KVT + cb * ROWS * 128, &tmV, &full[s], cb * (128 / C::ES), (int)tl.ph,
+                          (int)kv0, (int)b);
+            }
+          }
+        } else if (role == 1) {
+          // cos / sin rows of the tile's logical slots; lane: chunk c = lane % 16 of rows
+          // lane/16 + 2i, swizzled by tbl_swz
+          const int c = lane & 15, r0 = lane >> 4;
+          const uint32_t tbase = sbase + 2 * C::SCT;
+          const float *cs = p.cosT + (uint64_t)cur * (kD / 2) + c * 4, *sn = p.sinT + (uint64_t)cur * (kD / 2) + c * 4;
+#pragma unroll
+          for (int i = 0; i < TP / 2; ++i) {
+            const int r = r0 + 2 * i;
             const bool valid = (uint32_t)r < tl.n;
-            const uint64_t row = valid ? (((uint64_t)b * p.seq_stride + tl.ph + r) * p.KV + kv0 + hh) : 0;
-            const float *src = (which ? p.Vsp : p.Ksp) + row * NB;
-            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(sbase + which * C::SCT + rem * 16),
-                         "l"(src), "r"(valid ? 16u : 0u)
+            const uint32_t off = valid ? r * (kD / 2) : 0;
+            const uint32_t dst = tbase + (r * 16 + (c ^ tbl_swz<MODE>(r))) * 16;
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(cs + off),
+                         "r"(valid ? 16u : 0u)
+                         : "memory");
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst + C::TBL), "l"(sn + off),
+                         "r"(valid ? 16u : 0u)
                          : "memory");
           }
-        }
-        // cos / sin rows of the tile's logical slots, 16-byte chunks swizzled by (slot & 7)
-        const uint32_t tbase = sbase + 2 * C::SCT;
-        for (int idx = lane; idx < 2 * TP * 16; idx += 32) {
-          const int which = idx / (TP * 16), rem = idx % (TP * 16);
-          const int r = rem / 16, c = rem % 16;
+          asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&full[s])) : "memory");
+        } else if constexpr (MODE == BG_KV_Q8) {
+          // block scales [head][slot][NB] of both caches (head-major: the 8 slots a consumer warp
+          // reads at once are 16 bytes apart); lane: slot lane % 16 of heads lane/16 + 2i; slots
+          // past the tile are zero-filled
+          const int r = lane & 15, h0 = lane >> 4;
           const bool valid = (uint32_t)r < tl.n;
-          const float *src = (which ? p.sinT : p.cosT) + (uint64_t)(valid ? cur + r : 0) * (kD / 2) + c * 4;
-          asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(tbase + which * C::TBL +
-                                                                            (r * 16 + (c ^ (r & 7))) * 16),
-                       "l"(src), "r"(valid ? 16u : 0u)
-                       : "memory");
+          const uint64_t row = valid ? ((uint64_t)b * p.seq_stride + tl.ph + r) * p.KV + kv0 : 0;
+          const float *ks = p.Ksp + row * NB, *vs = p.Vsp + row * NB;
+#pragma unroll
+          for (int i = 0; i < HPC / 2; ++i) {
+            const int hh = h0 + 2 * i;
+            const uint32_t dst = sbase + (hh * TP + r) * 16;
+            const uint32_t off = valid ? hh * NB : 0;
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(ks + off),
+                         "r"(valid ? 16u : 0u)
+                         : "memory");
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst + C::SCT), "l"(vs + off),
+                         "r"(valid ? 16u : 0u)
+                         : "memory");
+          }
+          asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&full[s])) : "memory");
         }
-        asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&full[s])) : "memory");
         cur += tl.n;
       }
       f = (uint64_t)pc.unit * p.L + (pc.e - p.pos_lo);
     }
     // never leave the CTA with copies in flight: wait (bounded) for the last stages
-    if (lane == 0 && ok)
+    if (role == 0 && lane == 0 && ok)
       for (uint32_t u = t > (uint32_t)NST ? t - NST : 0; u < t; ++u) mbar_wait(&full[u % NST], (u / NST) & 1);
     asm volatile("cp.async.wait_all;" ::: "memory");
     return;
   }
 
   // ---------------- consumer warps: warp w owns kv head kv0 + w ----------------
+  if constexpr (C::SPLIT_REGS) asm volatile("setmaxnreg.inc.sync.aligned.u32 232;" ::: "memory");
+  if (warp >= HPC) return;  // idle warps of a padded consumer warpgroup
   const int lrow = (((lane >> 3) & 1) << 3) + (lane & 7);
   const int lhi = lane >> 4;
   const int trow = ((lane >> 4) << 3) + (lane & 7);
@@ -270,40 +310,28 @@ __global__ void __launch_bounds__(RCfg<MODE, HPC>::THREADS, 1)
 #pragma unroll
       for (int i = 0; i < 4; ++i) oacc[mt][i] = 0.f;
 
-    for (uint32_t cur = pc.a; cur < pc.e && ok; ++t) {
-      const Tile tl = next_tile(p, cur, pc.e);
-      const int s = t % NST;
-      if (!mbar_wait_warp(&full[s], (t / NST) & 1)) {
-        ok = false;
-        break;
-      }
-      const uint32_t sb = smem_u32(smem + s * C::STAGE);
-      const uint32_t kb = sb, vb = sb + C::KVT;
+    // scores S^T = rot(K) . Q^T of one tile (raw, unscaled), one pair of k steps (dims d and
+    // d + D/2) at a time, into four independent accumulators that keep the MMA chains short.
+    // The rotation runs in packed f16: register slot i of an A fragment holds two consecutive
+    // dims of row a (i even) or b (i odd); its partner slot in step ks + KS/2 holds the same
+    // dims + D/2.  cos/sin are read as f32 from the staged slice and packed once per row and slot.
+    auto tile_scores = [&](uint32_t sb, const float *ksc, float (&acc)[4]) {
+      const uint32_t kb = sb;
       const uint32_t tcos = sb + 2 * C::KVT + 2 * C::SCT, tsin = tcos + C::TBL;
-      const float *ksc = reinterpret_cast<const float *>(smem + s * C::STAGE + 2 * C::KVT);
-      const uint32_t pa = cur + ra, pb = pa + 8;
-      const bool va_ok = (uint32_t)ra < tl.n, vb_ok = (uint32_t)(ra + 8) < tl.n;
-
-      // ---- scores S^T = rot(K) . Q^T, one pair of k steps (dims d, d + D/2) at a time ----
-      // four independent accumulators (one per pair of k steps) keep the MMA chains short
       float acc4[KS / 2][4];
 #pragma unroll
       for (int c = 0; c < KS / 2; ++c)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc4[c][i] = 0.f;
-#if BG_ROLL_ROT_F16
-      // Packed-f16 rotation: register slot i of an A fragment holds two consecutive dims of row a
-      // (i even) or b (i odd); its partner slot in step ks + KS/2 holds the same dims + D/2.
-      // cos/sin are read as f32 from the staged slice and packed once per row and slot.
       auto rotate_mma = [&](const uint32_t (&kl)[4], const uint32_t (&kh)[4], int ks) {
-        __half2 cs[4], sn[4], nsn[4];
+        __half2 cs[4], sn[4];
 #pragma unroll
         for (int rb = 0; rb < 2; ++rb) {
           const int r = ra + 8 * rb;
           if constexpr (MODE == BG_KV_F16) {
             const int c = ks * 4 + ((lane & 3) >> 1);  // dims d0 = ks*16 + 2*(lane&3) and d0 + 8
-            const uint32_t o0 = (r * 16 + (c ^ (r & 7))) * 16 + 8 * (lane & 1);
-            const uint32_t o1 = (r * 16 + ((c + 2) ^ (r & 7))) * 16 + 8 * (lane & 1);
+            const uint32_t o0 = (r * 16 + (c ^ tbl_swz<MODE>(r))) * 16 + 8 * (lane & 1);
+            const uint32_t o1 = (r * 16 + ((c + 2) ^ tbl_swz<MODE>(r))) * 16 + 8 * (lane & 1);
             float2 c0, c1, s0, s1;
             asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(c0.x), "=f"(c0.y) : "r"(tcos + o0));
             asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(c1.x), "=f"(c1.y) : "r"(tcos + o1));
@@ -315,7 +343,7 @@ __global__ void __launch_bounds__(RCfg<MODE, HPC>::THREADS, 1)
             sn[2 + rb] = __float22half2_rn(s1);
           } else {
             const int c = (ks >> 1) * 8 + (ks & 1) * 4 + (lane & 3);  // dims 4c .. 4c+3
-            const uint32_t o = (r * 16 + (c ^ (r & 7))) * 16;
+            const uint32_t o = (r * 16 + (c ^ tbl_swz<MODE>(r))) * 16;
             float4 c4, s4;
             asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
                          : "=f"(c4.x), "=f"(c4.y), "=f"(c4.z), "=f"(c4.w)
@@ -329,31 +357,29 @@ __global__ void __launch_bounds__(RCfg<MODE, HPC>::THREADS, 1)
             sn[2 + rb] = __floats2half2_rn(s4.z, s4.w);
           }
         }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) nsn[i] = __hneg2(sn[i]);
         uint32_t al[4], ah[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const __half2 lo_h = *reinterpret_cast<const __half2 *>(&kl[i]);
           const __half2 hi_h = *reinterpret_cast<const __half2 *>(&kh[i]);
-          const __half2 rl = __hfma2(hi_h, nsn[i], __hmul2(lo_h, cs[i]));  // k*cos - k[d+D/2]*sin
-          const __half2 rh = __hfma2(lo_h, sn[i], __hmul2(hi_h, cs[i]));   // k*cos + k[d-D/2]*sin
+          const __half2 rl = __hfma2(__hneg2(hi_h), sn[i], __hmul2(lo_h, cs[i]));  // k*cos - k[d+D/2]*sin
+          const __half2 rh = __hfma2(lo_h, sn[i], __hmul2(hi_h, cs[i]));           // k*cos + k[d-D/2]*sin
           al[i] = *reinterpret_cast<const uint32_t *>(&rl);
           ah[i] = *reinterpret_cast<const uint32_t *>(&rh);
         }
-        float (&acc)[4] = acc4[ks];
-        mma16816(acc, al, qh[ks][0], qh[ks][1]);
-        mma16816(acc, ah, qh[ks + KS / 2][0], qh[ks + KS / 2][1]);
-        mma16816(acc, al, ql[ks][0], ql[ks][1]);
-        mma16816(acc, ah, ql[ks + KS / 2][0], ql[ks + KS / 2][1]);
+        float (&ac)[4] = acc4[ks];
+        mma16816(ac, al, qh[ks][0], qh[ks][1]);
+        mma16816(ac, ah, qh[ks + KS / 2][0], qh[ks + KS / 2][1]);
+        mma16816(ac, al, ql[ks][0], ql[ks][1]);
+        mma16816(ac, ah, ql[ks + KS / 2][0], ql[ks + KS / 2][1]);
       };
       if constexpr (MODE == BG_KV_F16) {
 #pragma unroll
         for (int ks = 0; ks < KS / 2; ++ks) {
-          uint32_t a[4], a2[4];
-          ldsm_x4(a, swz<ROWS>(kb, row0 + lrow, 2 * ks + lhi));
-          ldsm_x4(a2, swz<ROWS>(kb, row0 + lrow, 2 * (ks + KS / 2) + lhi));
-          rotate_mma(a, a2, ks);
+          uint32_t x[4], x2[4];
+          ldsm_x4(x, swz<ROWS>(kb, row0 + lrow, 2 * ks + lhi));
+          ldsm_x4(x2, swz<ROWS>(kb, row0 + lrow, 2 * (ks + KS / 2) + lhi));
+          rotate_mma(x, x2, ks);
         }
       } else {
         // snorm8 read: max(code, -127) * (scale/127): the code becomes the exact f16 1152 + code
@@ -364,7 +390,7 @@ __global__ void __launch_bounds__(RCfg<MODE, HPC>::THREADS, 1)
           const __half2 v = __hmul2(__hsub2(__hmax2(*reinterpret_cast<const __half2 *>(&hb), lo127), bias), sc);
           return *reinterpret_cast<const uint32_t *>(&v);
         };
-        const int sa_i = (ra * HPC + warp) * NB, sb_i = ((ra + 8) * HPC + warp) * NB;
+        const int sa_i = (warp * TP + ra) * NB, sb_i = (warp * TP + ra + 8) * NB;
 #pragma unroll
         for (int bk = 0; bk < NB / 2; ++bk) {
           uint32_t r[4], r2[4];
@@ -390,159 +416,36 @@ __global__ void __launch_bounds__(RCfg<MODE, HPC>::THREADS, 1)
           }
         }
       }
-#else
-      auto rotate_mma = [&](float (&lo_f)[8], float (&hi_f)[8], int ks) {
-        float cr_[2][4], sr_[2][4];  // [row a/b][dim slot]
-#pragma unroll
-        for (int rb = 0; rb < 2; ++rb) {
-          const int r = ra + 8 * rb;
-          if constexpr (MODE == BG_KV_F16) {
-            const int c = ks * 4 + ((lane & 3) >> 1);  // dims d0 = ks*16 + 2*(lane&3) and d0 + 8
-            const uint32_t o0 = (r * 16 + (c ^ (r & 7))) * 16 + 8 * (lane & 1);
-            const uint32_t o1 = (r * 16 + ((c + 2) ^ (r & 7))) * 16 + 8 * (lane & 1);
-            float2 c0, c1, s0, s1;
-            asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(c0.x), "=f"(c0.y) : "r"(tcos + o0));
-            asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(c1.x), "=f"(c1.y) : "r"(tcos + o1));
-            asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(s0.x), "=f"(s0.y) : "r"(tsin + o0));
-            asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(s1.x), "=f"(s1.y) : "r"(tsin + o1));
-            cr_[rb][0] = c0.x; cr_[rb][1] = c0.y; cr_[rb][2] = c1.x; cr_[rb][3] = c1.y;
-            sr_[rb][0] = s0.x; sr_[rb][1] = s0.y; sr_[rb][2] = s1.x; sr_[rb][3] = s1.y;
-          } else {
-            const int c = (ks >> 1) * 8 + (ks & 1) * 4 + (lane & 3);  // dims 4c .. 4c+3
-            const uint32_t o = (r * 16 + (c ^ (r & 7))) * 16;
-            float4 c4, s4;
-            asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
-                         : "=f"(c4.x), "=f"(c4.y), "=f"(c4.z), "=f"(c4.w)
-                         : "r"(tcos + o));
-            asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
-                         : "=f"(s4.x), "=f"(s4.y), "=f"(s4.z), "=f"(s4.w)
-                         : "r"(tsin + o));
-            cr_[rb][0] = c4.x; cr_[rb][1] = c4.y; cr_[rb][2] = c4.z; cr_[rb][3] = c4.w;
-            sr_[rb][0] = s4.x; sr_[rb][1] = s4.y; sr_[rb][2] = s4.z; sr_[rb][3] = s4.w;
-          }
-        }
-        float rl[8], rh[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          // element e: {a0.x, a0.y, a1.x, a1.y, a2.x, a2.y, a3.x, a3.y}; a1/a3 hold row b
-          const int rb = (e >> 1) & 1;
-          const int slot = ((e >> 2) & 1) * 2 + (e & 1);
-          const float c = cr_[rb][slot], sn = sr_[rb][slot];
-          rl[e] = lo_f[e] * c - hi_f[e] * sn;  // d < D/2: k*cos + (-k[d+D/2])*sin
-          rh[e] = hi_f[e] * c + lo_f[e] * sn;  // d >= D/2: k*cos + k[d-D/2]*sin
-        }
-        const uint32_t al[4] = {pack_f16(rl[0], rl[1]), pack_f16(rl[2], rl[3]), pack_f16(rl[4], rl[5]),
-                                pack_f16(rl[6], rl[7])};
-        const uint32_t ah[4] = {pack_f16(rh[0], rh[1]), pack_f16(rh[2], rh[3]), pack_f16(rh[4], rh[5]),
-                                pack_f16(rh[6], rh[7])};
-        float (&acc)[4] = acc4[ks];
-        mma16816(acc, al, qh[ks][0], qh[ks][1]);
-        mma16816(acc, ah, qh[ks + KS / 2][0], qh[ks + KS / 2][1]);
-        mma16816(acc, al, ql[ks][0], ql[ks][1]);
-        mma16816(acc, ah, ql[ks + KS / 2][0], ql[ks + KS / 2][1]);
-      };
-      if constexpr (MODE == BG_KV_F16) {
-#pragma unroll
-        for (int ks = 0; ks < KS / 2; ++ks) {
-          uint32_t a[4], a2[4];
-          ldsm_x4(a, swz<ROWS>(kb, row0 + lrow, 2 * ks + lhi));
-          ldsm_x4(a2, swz<ROWS>(kb, row0 + lrow, 2 * (ks + KS / 2) + lhi));
-          float lo_f[8], hi_f[8];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float2 x = __half22float2(*reinterpret_cast<const __half2 *>(&a[i]));
-            const float2 y = __half22float2(*reinterpret_cast<const __half2 *>(&a2[i]));
-            lo_f[2 * i] = x.x;
-            lo_f[2 * i + 1] = x.y;
-            hi_f[2 * i] = y.x;
-            hi_f[2 * i + 1] = y.y;
-          }
-          rotate_mma(lo_f, hi_f, ks);
-        }
-      } else {
-        // snorm8 read: max(code/127, -1) * scale == max(code, -127) * (scale/127)
-        const int sa_i = (ra * HPC + warp) * NB, sb_i = ((ra + 8) * HPC + warp) * NB;
-#pragma unroll
-        for (int bk = 0; bk < NB / 2; ++bk) {
-          uint32_t r[4], r2[4];
-          ldsm_x4(r, swz<ROWS>(kb, row0 + lrow, 2 * bk + lhi));
-          ldsm_x4(r2, swz<ROWS>(kb, row0 + lrow, 2 * (bk + NB / 2) + lhi));
-          const float s0 = ksc[sa_i + bk] * (1.0f / 127.0f), s1 = ksc[sb_i + bk] * (1.0f / 127.0f);
-          const float t0 = ksc[sa_i + bk + NB / 2] * (1.0f / 127.0f), t1 = ksc[sb_i + bk + NB / 2] * (1.0f / 127.0f);
-#pragma unroll
-          for (int h2 = 0; h2 < 2; ++h2) {  // k step 2bk + h2 from words r[2h2] (row a), r[2h2+1] (row b)
-            const uint32_t wa = r[2 * h2], wb = r[2 * h2 + 1], xa = r2[2 * h2], xb = r2[2 * h2 + 1];
-            float lo_f[8], hi_f[8];
-            // a0 = bytes 0,1 of row a; a1 = bytes 0,1 of row b; a2 = bytes 2,3 of row a; a3 = row b
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const int sh = 8 * ((e & 1) + 2 * (e >> 2));
-              const bool rowb = (e >> 1) & 1;
-              lo_f[e] = fmaxf((float)(int8_t)(((rowb ? wb : wa) >> sh) & 0xff), -127.f) * (rowb ? s1 : s0);
-              hi_f[e] = fmaxf((float)(int8_t)(((rowb ? xb : xa) >> sh) & 0xff), -127.f) * (rowb ? t1 : t0);
-            }
-            rotate_mma(lo_f, hi_f, 2 * bk + h2);
-          }
-        }
-      }
-
-#endif
-      float acc[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[i] = (acc4[0][i] + acc4[1][i]) + (acc4[2][i] + acc4[3][i]);
+    };
 
-      // ---- online softmax (columns n0 = 2(lane%4), n1 = n0+1; rows pa, pb) ----
-      float pr[4], cr[2];
-      bool moved = false;
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const float x0 = (va_ok && pa <= lim[j]) ? acc[j] * p.sl2 : -INFINITY;
-        const float x1 = (vb_ok && pb <= lim[j]) ? acc[2 + j] * p.sl2 : -INFINITY;
-        float mx = fmaxf(x0, x1);
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-        const float mn = fmaxf(m[j], mx);
-        const float corr = exp2f(m[j] - mn);
-        const float p0 = exp2f(x0 - mn), p1 = exp2f(x1 - mn);
-        l[j] = l[j] * corr + p0 + p1;
-        m[j] = mn;
-        pr[j] = p0;
-        pr[2 + j] = p1;
-        cr[j] = corr;
-        moved |= corr != 1.0f;
-      }
-      if (__any_sync(0xffffffffu, moved)) {
-#pragma unroll
-        for (int mt = 0; mt < KS; ++mt)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) oacc[mt][i] *= cr[i & 1];
-      }
-
-      // ---- O^T += V^T . P^T ----
+    // O^T += V^T . P^T of one tile
+    auto tile_pv = [&](uint32_t sb, const float *ksc, uint32_t n, const float (&pr)[4]) {
+      const uint32_t vb = sb + C::KVT;
       if constexpr (MODE == BG_KV_F16) {
         const uint32_t pb0 = movm_t(pack_f16(pr[0], pr[1])), pb1 = movm_t(pack_f16(pr[2], pr[3]));
         // slots past a short tile may hold any bits (another run of the ring): zero them so that
         // 0 * NaN cannot reach the accumulator.  Fragment halves: slots 2(lane%4)+{0,1} (+8).
         uint32_t mlo = 0xffffffffu, mhi = 0xffffffffu;
-        if (tl.n < (uint32_t)TP) {
+        if (n < (uint32_t)TP) {
           const uint32_t k0 = 2 * (lane & 3);
-          mlo = (k0 < tl.n ? 0xffffu : 0u) | (k0 + 1 < tl.n ? 0xffff0000u : 0u);
-          mhi = (k0 + 8 < tl.n ? 0xffffu : 0u) | (k0 + 9 < tl.n ? 0xffff0000u : 0u);
+          mlo = (k0 < n ? 0xffffu : 0u) | (k0 + 1 < n ? 0xffff0000u : 0u);
+          mhi = (k0 + 8 < n ? 0xffffu : 0u) | (k0 + 9 < n ? 0xffff0000u : 0u);
         }
 #pragma unroll
         for (int mt = 0; mt < KS; ++mt) {
-          uint32_t a[4];
-          ldsm_x4_t(a, swz<ROWS>(vb, row0 + trow, 2 * mt + tcol));
-          a[0] &= mlo;
-          a[1] &= mlo;
-          a[2] &= mhi;
-          a[3] &= mhi;
-          mma16816(oacc[mt], a, pb0, pb1);
+          uint32_t x[4];
+          ldsm_x4_t(x, swz<ROWS>(vb, row0 + trow, 2 * mt + tcol));
+          x[0] &= mlo;
+          x[1] &= mlo;
+          x[2] &= mhi;
+          x[3] &= mhi;
+          mma16816(oacc[mt], x, pb0, pb1);
         }
       } else {
         const float *vsc = ksc + TP * HPC * NB;
-        const int sa_i = (ra * HPC + warp) * NB, sb_i = ((ra + 8) * HPC + warp) * NB;
+        const int sa_i = (warp * TP + ra) * NB, sb_i = (warp * TP + ra + 8) * NB;
 #pragma unroll
         for (int bk = 0; bk < NB; ++bk) {
           const float va = vsc[sa_i + bk] * (1.0f / 127.0f);  // zero-filled past the tile
@@ -565,9 +468,92 @@ __global__ void __launch_bounds__(RCfg<MODE, HPC>::THREADS, 1)
           mma16816(oacc[2 * bk + 1], aneg, pb0, pb1);
         }
       }
+    };
+
+    // NSUB (1 or 2) consecutive tiles per step: one max reduction and one rescale decision per
+    // column for up to 32 slots, and two independent score chains in flight.
+    auto step = [&](auto nsub_c, const uint32_t (&cu)[2], const Tile (&tl)[2], const int (&st)[2]) {
+      constexpr int NSUB = decltype(nsub_c)::value;
+#ifdef BG_EXP_NOCOMPUTE
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
-      cur += tl.n;
+      if (lane == 0)
+        for (int u = 0; u < NSUB; ++u) mbar_arrive(&empty[st[u]]);
+      return;
+#endif
+      float acc[NSUB][4];
+#pragma unroll
+      for (int u = 0; u < NSUB; ++u)
+        tile_scores(smem_u32(smem + st[u] * C::STAGE),
+                    reinterpret_cast<const float *>(smem + st[u] * C::STAGE + 2 * C::KVT), acc[u]);
+      float pr[NSUB][4], cr[2];
+      bool moved = false;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        float x[NSUB][2];
+        float mx = -INFINITY;
+#pragma unroll
+        for (int u = 0; u < NSUB; ++u) {
+          const uint32_t pa = cu[u] + ra;
+          x[u][0] = ((uint32_t)ra < tl[u].n && pa <= lim[j]) ? acc[u][j] * p.sl2 : -INFINITY;
+          x[u][1] = ((uint32_t)(ra + 8) < tl[u].n && pa + 8 <= lim[j]) ? acc[u][2 + j] * p.sl2 : -INFINITY;
+          mx = fmaxf(mx, fmaxf(x[u][0], x[u][1]));
+        }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        const float mn = fmaxf(m[j], mx);
+        const float corr = exp2f(m[j] - mn);
+        float ls = 0.f;
+#pragma unroll
+        for (int u = 0; u < NSUB; ++u) {
+          pr[u][j] = exp2f(x[u][0] - mn);
+          pr[u][2 + j] = exp2f(x[u][1] - mn);
+          ls += pr[u][j] + pr[u][2 + j];
+        }
+        l[j] = l[j] * corr + ls;
+        m[j] = mn;
+        cr[j] = corr;
+        moved |= corr != 1.0f;
+      }
+      if (__any_sync(0xffffffffu, moved)) {
+#pragma unroll
+        for (int mt = 0; mt < KS; ++mt)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) oacc[mt][i] *= cr[i & 1];
+      }
+#pragma unroll
+      for (int u = 0; u < NSUB; ++u)
+        tile_pv(smem_u32(smem + st[u] * C::STAGE),
+                reinterpret_cast<const float *>(smem + st[u] * C::STAGE + 2 * C::KVT), tl[u].n, pr[u]);
+      __syncwarp();
+      if (lane == 0)
+#pragma unroll
+        for (int u = 0; u < NSUB; ++u) mbar_arrive(&empty[st[u]]);
+    };
+
+    for (uint32_t cur = pc.a; cur < pc.e && ok;) {
+      Tile tl[2];
+      uint32_t cu[2];
+      cu[0] = cur;
+      tl[0] = next_tile(p, cur, pc.e);
+      cu[1] = cur + tl[0].n;
+      const bool two = cu[1] < pc.e;
+      tl[1] = two ? next_tile(p, cu[1], pc.e) : Tile{0u, 0u};
+      const int st[2] = {(int)(t % NST), (int)((t + 1) % NST)};
+      if (!mbar_wait_warp(&full[st[0]], (t / NST) & 1) ||
+          (two && !mbar_wait_warp(&full[st[1]], ((t + 1) / NST) & 1))) {
+        ok = false;
+        break;
+      }
+      if (two) {
+        step(std::integral_constant<int, 2>{}, cu, tl, st);
+        t += 2;
+        cur = cu[1] + tl[1].n;
+      } else {
+        step(std::integral_constant<int, 1>{}, cu, tl, st);
+        t += 1;
+        cur = cu[1];
+      }
     }
 
     // ---- piece epilogue: this head's rows (columns) to the partial slot or the final output ----
