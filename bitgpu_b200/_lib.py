@@ -19,7 +19,7 @@ EXPORTS = [
     "bg_lse_merge", "bg_kv_append", "bg_kv_append_kv", "bg_rmsnorm_rope", "bg_kv_evict", "bg_kv_ring_evict",
     "bg_deltanet_gbeta", "bg_deltanet_recur", "bg_deltanet_norm_gate", "bg_deltanet_fused",
     "bg_gate_sigmoid", "bg_attention_noalloc", "bg_deltanet_chunked_workspace_size",
-    "bg_deltanet_chunked",
+    "bg_deltanet_chunked", "bg_qk_norm_rope", "bg_conv1d_causal", "bg_slice_cols",
 ]
 
 
@@ -56,6 +56,10 @@ _SIGS = {
     "bg_lse_merge": (C.c_int, [P, U32, U32, U32, P, P, U32, P]),
     "bg_kv_append": (C.c_int, [C.POINTER(KVCacheDesc), U32, U32, P, U32, U32, U32, U32, U32, P]),
     "bg_kv_append_kv": (C.c_int, [C.POINTER(KVCacheDesc), U32, P, P, U32, U32, U32, U32, U32, P]),
+    "bg_qk_norm_rope": (C.c_int, [P, U32, U32, U32, U32, U32, U32, P, P, P, U32, U32, F, P,
+                                  C.POINTER(KVCacheDesc), P]),
+    "bg_conv1d_causal": (C.c_int, [P, P, P, U32, U32, U32, U32, P, P, P]),
+    "bg_slice_cols": (C.c_int, [P, U32, U32, U32, U32, P, P]),
     "bg_rmsnorm_rope": (C.c_int, [P, U32, U32, U32, P, P, P, F, P, C.POINTER(KVCacheDesc), U32, P]),
     "bg_kv_evict": (C.c_int, [C.POINTER(KVCacheDesc), U32, U32, U32, U32, U32, U32, C.POINTER(U32), P]),
     "bg_kv_ring_evict": (C.c_int, [C.POINTER(KVCacheDesc), U32, U32, U32, C.POINTER(U32)]),

@@ -238,6 +238,42 @@ int bg_kv_append_kv(const bg_kv_cache *kv, uint32_t batch, const void *k_src, co
                           pos0, 0, 2, (cudaStream_t)stream);
 }
 
+int bg_qk_norm_rope(const float *x, uint32_t batch, uint32_t S, uint32_t heads, uint32_t D, uint32_t x_stride,
+                    uint32_t x_off, const float *gamma, const float *cosT, const float *sinT, uint32_t rot,
+                    uint32_t pos0, float eps, float *y, const bg_kv_cache *kv, bg_stream_t stream) {
+  if (!x || !gamma || (!y && !kv) || rot > D || rot % 2 || (rot && (!cosT || !sinT))) return BG_EINVAL;
+  if (!d_ok(D)) return BG_EUNSUPPORTED;
+  if (x_stride < D || (uint64_t)x_off + D > x_stride || heads == 0) return BG_EINVAL;
+  KVView v = {};
+  int mode = 0;
+  if (kv) {
+    if (!kv_mode_ok(kv->mode) || !kv->K) return BG_EINVAL;
+    if ((kv->mode == BG_KV_Q8 || kv->mode == BG_KV_Q8R) && !kv->Ks) return BG_EINVAL;
+    if (kv->mode == BG_KV_Q8R && D % 128) return BG_EINVAL;
+    const uint64_t cap = kv->window ? (uint64_t)kv->sinks + kv->window : kv->seq_stride;
+    if ((uint64_t)pos0 + S > cap) return BG_EINVAL;
+    v = make_view(kv, heads, 0);
+    mode = (int)kv->mode;
+  }
+  if (batch == 0 || S == 0) return BG_OK;
+  return launch_qk_norm_rope(x, batch, S, heads, D, x_stride, x_off, gamma, cosT, sinT, rot, pos0, eps, y, v, mode,
+                             kv != nullptr, (cudaStream_t)stream);
+}
+
+int bg_conv1d_causal(const float *x, const float *w, const float *state_in, uint32_t load_state, uint32_t S,
+                     uint32_t C, uint32_t K, float *y, float *state_out, bg_stream_t stream) {
+  if ((!x && S) || !w || (!y && S) || !state_out || C == 0 || K < 2) return BG_EINVAL;
+  if (load_state && (!state_in || state_in == state_out)) return BG_EINVAL;  // the engine ping-pongs them
+  if (K > 8) return BG_EUNSUPPORTED;
+  return launch_conv1d_causal(x, w, state_in, load_state != 0, S, C, K, y, state_out, (cudaStream_t)stream);
+}
+
+int bg_slice_cols(const float *src, uint32_t rows, uint32_t width, uint32_t stride, uint32_t off, float *dst,
+                  bg_stream_t stream) {
+  if (!src || !dst || (uint64_t)off + width > stride) return BG_EINVAL;
+  return launch_slice_cols(src, rows, width, stride, off, dst, (cudaStream_t)stream);
+}
+
 int bg_rmsnorm_rope(const float *x, uint32_t batch, uint32_t R, uint32_t D, const float *gamma, const float *cos,
                     const float *sin, float eps, float *y, const bg_kv_cache *kv, uint32_t pos, bg_stream_t stream) {
   if (!x || !gamma || (!y && !kv) || ((cos == nullptr) != (sin == nullptr))) return BG_EINVAL;

@@ -12,6 +12,14 @@ int launch_rmsnorm_rope(const float *x, uint32_t B, uint32_t R, uint32_t D, cons
                         cudaStream_t st);
 // Copy nbytes within each of B sequence slabs (slab i at base + i*seq_bytes) from src_off to
 // dst_off; the ranges must not overlap.
+int launch_qk_norm_rope(const float *x, uint32_t B, uint32_t S, uint32_t heads, uint32_t D, uint32_t x_stride,
+                        uint32_t x_off, const float *gamma, const float *cosT, const float *sinT, uint32_t rot,
+                        uint32_t pos0, float eps, float *y, const KVView &kv, int mode, int to_cache,
+                        cudaStream_t st);
+int launch_conv1d_causal(const float *x, const float *w, const float *state_in, int load_state, uint32_t S,
+                         uint32_t C, uint32_t K, float *y, float *state_out, cudaStream_t st);
+int launch_slice_cols(const float *src, uint32_t rows, uint32_t width, uint32_t stride, uint32_t off, float *dst,
+                      cudaStream_t st);
 int launch_copy_rows(void *base, uint64_t seq_bytes, uint32_t B, uint64_t dst_off, uint64_t src_off, uint64_t nbytes,
                      cudaStream_t st);
 

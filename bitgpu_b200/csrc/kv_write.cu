@@ -141,6 +141,60 @@ __global__ void copy_rows_kernel(uint8_t *base, uint64_t seq_bytes, uint64_t dst
   }
 }
 
+// The gated-attention prologue of engine.ts:1471-1485 for one head row (b, s, h), one warp:
+// split_head (the row is read at x + ((b*S + s)*heads + h)*x_stride + x_off), the plain RMSNorm
+// with its baked scale (rms, y = x * rsqrt(mean(x^2) + eps) * gamma), rope_partial.wgsl:12-24
+// (rotate_half inside the first `rot` dims, tables [pos][rot] at row pos0 + s, the rest passes
+// through) and optionally the cache write of the result at logical position pos0 + s (appendKV).
+template <int DPL>
+__global__ void qk_norm_rope_kernel(const float *x, uint32_t B, uint32_t S, uint32_t heads, uint32_t x_stride,
+                                    uint32_t x_off, const float *gamma, const float *cosT, const float *sinT,
+                                    uint32_t rot, uint32_t pos0, float eps, float *y, KVView kv, int mode,
+                                    int to_cache) {
+  constexpr int D = DPL * 32;
+  const uint32_t gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= B * S * heads) return;
+  const float *src = x + (uint64_t)gw * x_stride + x_off;
+  float v[DPL], g[DPL];
+#pragma unroll
+  for (int i = 0; i < DPL; ++i) {
+    v[i] = src[lane * DPL + i];
+    g[i] = gamma[lane * DPL + i];
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < DPL; ++i) ss = fmaf(v[i], v[i], ss);
+  ss = warp_sum(ss);
+  const float inv = 1.0f / sqrtf(ss / (float)D + eps);
+  const uint32_t s = (gw / heads) % S;
+  const uint32_t half = rot / 2;
+  float out[DPL];
+#pragma unroll
+  for (int i = 0; i < DPL; ++i) {
+    const uint32_t d = lane * DPL + i;
+    const float nd = v[i] * inv * g[i];
+    if (d < rot) {
+      const uint32_t pd = d < half ? d + half : d - half;
+      const float np = src[pd] * inv * gamma[pd];
+      const float rv = d < half ? -np : np;
+      const uint64_t t = (uint64_t)(pos0 + s) * rot + d;
+      out[i] = nd * cosT[t] + rv * sinT[t];
+    } else {
+      out[i] = nd;
+    }
+  }
+  if (y) {
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) y[(uint64_t)gw * D + lane * DPL + i] = out[i];
+  }
+  if (to_cache) {
+    const uint32_t h = gw % heads, b = gw / (heads * S);
+    const uint64_t row = cache_row(kv, b, pos0 + s, h);
+    store_row<DPL>(const_cast<void *>(kv.K), const_cast<float *>(kv.Ks), mode, row, lane, out);
+  }
+}
+
 template <int DPL>
 int launch_append_d(const KVView &kv, int mode, const void *src0, const void *src1, int f16, uint32_t B, uint32_t S,
                     uint32_t pos0, int first_v, int nsides, cudaStream_t st) {
@@ -173,6 +227,25 @@ int launch_rmsnorm_rope(const float *x, uint32_t B, uint32_t R, uint32_t D, cons
     case 256: rmsnorm_rope_kernel<8><<<blocks, 128, 0, st>>>(x, B, R, gamma, cosv, sinv, eps, y, kv, mode, pos, to_cache); break;
     default: return BG_EUNSUPPORTED;
   }
+  return cudaGetLastError() == cudaSuccess ? BG_OK : BG_ELAUNCH;
+}
+
+int launch_qk_norm_rope(const float *x, uint32_t B, uint32_t S, uint32_t heads, uint32_t D, uint32_t x_stride,
+                        uint32_t x_off, const float *gamma, const float *cosT, const float *sinT, uint32_t rot,
+                        uint32_t pos0, float eps, float *y, const KVView &kv, int mode, int to_cache,
+                        cudaStream_t st) {
+  const uint64_t warps = (uint64_t)B * S * heads;
+  const uint32_t blocks = (uint32_t)((warps * 32 + 127) / 128);
+#define BG_QKNR(DPL_)                                                                                        \
+  qk_norm_rope_kernel<DPL_><<<blocks, 128, 0, st>>>(x, B, S, heads, x_stride, x_off, gamma, cosT, sinT, rot, \
+                                                    pos0, eps, y, kv, mode, to_cache)
+  switch (D) {
+    case 64: BG_QKNR(2); break;
+    case 128: BG_QKNR(4); break;
+    case 256: BG_QKNR(8); break;
+    default: return BG_EUNSUPPORTED;
+  }
+#undef BG_QKNR
   return cudaGetLastError() == cudaSuccess ? BG_OK : BG_ELAUNCH;
 }
 

@@ -247,6 +247,43 @@ def deltanet_chunked(q, k, v, a, b, a_neg, dt_bias, z, gamma, eps, state_in=None
     return y, state_out, core
 
 
+def conv1d_causal(x, w, state_in=None, state_out=None):
+    """``conv1d_causal`` (engine.ts:1422-1427): depthwise causal conv + SiLU of ``x[S, C]`` with
+    ``w[C, K]`` after the carried ``state_in[K-1, C]`` (None: zero left pad).
+    Returns ``(y[S, C], state_out[K-1, C])``."""
+    _need(x, torch.float32, "x")
+    _need(w, torch.float32, "w")
+    S, Cc = x.shape
+    K = w.shape[1]
+    y = torch.empty_like(x)
+    if state_out is None:
+        state_out = torch.empty((K - 1, Cc), dtype=torch.float32, device=x.device)
+    check("bg_conv1d_causal", lib().bg_conv1d_causal(_p(x), _p(w), _p(state_in), int(state_in is not None), S, Cc,
+                                                      K, _p(y), _p(state_out), _stream()))
+    return y, state_out
+
+
+def slice_cols(src, rows, width, stride, off):
+    """``slice_cols`` / ``split_head``: ``dst[r, c] = src.flat[r*stride + off + c]`` -> ``[rows, width]``."""
+    _need(src, torch.float32, "src")
+    dst = torch.empty((rows, width), dtype=torch.float32, device=src.device)
+    check("bg_slice_cols", lib().bg_slice_cols(_p(src), rows, width, stride, off, _p(dst), _stream()))
+    return dst
+
+
+def qk_norm_rope(x, batch, S, heads, D, x_stride, x_off, gamma, cos, sin, rot, pos0, eps, cache=None, want_y=True):
+    """The gated-attention prologue (engine.ts:1471-1485): split_head row read, RMSNorm with the
+    baked scale ``gamma``, partial RoPE over the first ``rot`` dims (tables ``[pos][rot]`` at row
+    ``pos0 + s``); returns ``y[batch, S, heads, D]`` (when ``want_y``) and/or writes the cache."""
+    _need(x, torch.float32, "x")
+    y = torch.empty((batch, S, heads, D), dtype=torch.float32, device=x.device) if want_y else None
+    d = cache.desc() if cache is not None else None
+    check("bg_qk_norm_rope", lib().bg_qk_norm_rope(_p(x), batch, S, heads, D, x_stride, x_off, _p(gamma), _p(cos),
+                                                    _p(sin), rot, pos0, float(eps), _p(y),
+                                                    C.byref(d) if d is not None else None, _stream()))
+    return y
+
+
 def gate_sigmoid(x, gate):
     y = torch.empty_like(x)
     check("bg_gate_sigmoid", lib().bg_gate_sigmoid(_p(x), _p(gate), x.numel(), _p(y), _stream()))

@@ -132,6 +132,37 @@ int bg_kv_append_kv(const bg_kv_cache *kv, uint32_t batch, const void *k_src, co
                     uint32_t src_dtype, uint32_t S, uint32_t KV, uint32_t D, uint32_t pos0,
                     bg_stream_t stream);
 
+/* bg_qk_norm_rope: the gated-attention prologue of engine.ts:1471-1485 in one launch, for
+ * batch x S x heads head rows of width D:
+ *   split_head.wgsl  row (b, s, h) is read at x + ((b*S + s)*heads + h)*x_stride + x_off
+ *                    (x_stride = 2*D, x_off = 0 picks the query half of the doubled q_proj);
+ *   rms              y = x * rsqrt(mean(x^2) + eps) * gamma (gamma = the baked (1 + w) scale);
+ *   rope_partial.wgsl rotate_half inside the first `rot` dims with the tables cosT/sinT
+ *                    [positions][rot] at row pos0 + s; dims >= rot pass through (rot = 0: none).
+ * The result goes to y [batch][S][heads][D] when y != NULL and/or into the cache's K at logical
+ * positions pos0 .. pos0+S-1 (heads == the cache's kv heads), with the cache's codec (the
+ * appendKV that follows it in the engine). */
+int bg_qk_norm_rope(const float *x, uint32_t batch, uint32_t S, uint32_t heads, uint32_t D,
+                    uint32_t x_stride, uint32_t x_off, const float *gamma, const float *cosT,
+                    const float *sinT, uint32_t rot, uint32_t pos0, float eps, float *y,
+                    const bg_kv_cache *kv, bg_stream_t stream);
+
+/* ---- hybrid-layer glue --------------------------------------------------------------------
+ * bg_conv1d_causal: conv1d_causal.wgsl (engine.ts:1422-1427).  Depthwise causal conv + SiLU over
+ * ext = [state_in (K-1 rows, zeros unless load_state); x (S rows)]:
+ *   y[t][c] = silu(sum_{j<K} w[c][j] * ext[t+j][c]),  state_out[i][c] = ext[S+i][c] (i < K-1).
+ * x, y [S][C]; w [C][K]; state_in, state_out [K-1][C] and distinct (the engine ping-pongs them).
+ * K <= 8. */
+int bg_conv1d_causal(const float *x, const float *w, const float *state_in, uint32_t load_state,
+                     uint32_t S, uint32_t C, uint32_t K, float *y, float *state_out,
+                     bg_stream_t stream);
+
+/* bg_slice_cols: slice_cols.wgsl (engine.ts:1428-1430) and split_head.wgsl (engine.ts:1473-1474):
+ * dst[r][c] = src[r*stride + off + c] for r < rows, c < width (off + width <= stride).
+ * split_head(S, H, Dh, off) == bg_slice_cols(src, S*H, Dh, 2*Dh, off, dst). */
+int bg_slice_cols(const float *src, uint32_t rows, uint32_t width, uint32_t stride, uint32_t off,
+                  float *dst, bg_stream_t stream);
+
 /* bg_rmsnorm_rope: rmsnorm_rope_sg{,_kv16,_kv8}.wgsl (engine.ts:1529-1540): per head row
  * y = rmsnorm(x)*gamma rotated by (cos, sin) ([D] tables of this position; NULL/NULL = no
  * rotation, the sink-mode cos=1/sin=0 binding of engine.ts:1533).  x [batch][R][D]; the result

@@ -15,4 +15,4 @@ the reference (no runnable CPU code there), so those restatements are "parity un
 kernel level: they follow the cited shader / engine lines and are cross-checked for
 internal consistency (f32 roll path == plain path before the first eviction, etc.).
 """
-from . import attention, deltanet, evict, kvcodec, rope  # noqa: F401
+from . import attention, deltanet, evict, glue, hybrid, kvcodec, rope  # noqa: F401

@@ -10,7 +10,9 @@ temporary folder and stores each case's inputs / expected outputs as float32 ``.
 (2) calls ``tools/qwen35_numpy.py`` directly for larger delta-rule cases (recurrent and
 chunked) and for gated / plain causal attention at head_dim 256 and 128 (through
 ``_full_attention`` with an identity hidden state and identity output projection, so the
-expected array is exactly the gated attention output the kernels must produce).
+expected array is exactly the gated attention output the kernels must produce); (3) runs the
+reference's q/k prologue functions and its whole hybrid ``forward`` on seeded dense weights
+(``oracle.hybrid.synth_weights``) for the end-to-end check.
 """
 import glob
 import json
@@ -84,6 +86,40 @@ def main(ref):
     gated_case("ga_d256_gated", S=13, H=6, KV=2, HD=256, rot=64, theta=1e7, gate_bias=0.0)
     # gate bias +100 makes sigmoid(gate) == 1.0 exactly in f32: plain causal GQA attention, D=128
     gated_case("ga_d128_plain", S=11, H=8, KV=4, HD=128, rot=128, theta=1e6, gate_bias=100.0)
+
+
+    # (2c) the fused q/k prologue: split_head -> rmsnorm (1 + w) -> rope_partial, through the
+    # reference's own rmsnorm / _rope_partial (engine.ts:1471-1485 dispatches them separately)
+    S, H, HD, ROT = 7, 3, 256, 64
+    Cp = qn.Qwen35Cfg(hidden=0, n_layers=0, eps=1e-6, n_heads=H, n_kv_heads=H, head_dim=HD, rot_dim=ROT,
+                      rope_theta=1e7, n_k_heads=1, n_v_heads=1, k_dim=1, v_dim=1, conv_kernel=4)
+    qg = rng.standard_normal((S, H, 2 * HD)).astype(np.float32)
+    wq = (0.1 * rng.standard_normal(HD)).astype(np.float32)
+    cos, sin = qn._rope_tables(Cp, S)
+    exp_q = qn._rope_partial(qn.rmsnorm(qg[..., :HD], wq, Cp.eps), cos, sin, ROT)
+    np.savez_compressed(os.path.join(HERE, "kc_qk_prologue.npz"), qg=qg, w=wq, cos=cos, sin=sin,
+                        expected=exp_q.astype(np.float32), gate=qg[..., HD:].copy())
+    print("wrote kc_qk_prologue.npz")
+
+    # (2d) end to end: the reference's numpy hybrid forward (tools/qwen35_numpy.py:216-237,
+    # "tile" value-head pairing as in the engine) on seeded dense weights with the synthetic
+    # model's dimensions (oracle.hybrid.synth_weights draws them; the test redraws the same).
+    sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+    from oracle import hybrid as HY
+    cfg = HY.Cfg()
+    seed, S = 7, 300
+    W = HY.synth_weights(cfg, seed)
+    ids = np.random.default_rng(11).integers(0, cfg.vocab, S).astype(np.int32)
+    Cf = qn.Qwen35Cfg(hidden=cfg.hidden, n_layers=cfg.n_layers, eps=cfg.eps, n_heads=cfg.n_heads,
+                      n_kv_heads=cfg.n_kv_heads, head_dim=cfg.head_dim, rot_dim=cfg.rot_dim, rope_theta=cfg.theta,
+                      n_k_heads=cfg.n_k_heads, n_v_heads=cfg.n_v_heads, k_dim=cfg.k_dim, v_dim=cfg.v_dim,
+                      conv_kernel=cfg.conv_k)
+    ref = qn.forward(W, Cf, ids, delta="chunk", repeat="tile")
+    np.savez_compressed(os.path.join(HERE, "hy_forward_s300.npz"), seed=np.int64(seed), ids=ids,
+                        logits_tail=ref["logits"][-16:].astype(np.float32),
+                        argmax=ref["logits"].argmax(-1).astype(np.int32),
+                        last_hidden=np.stack([h[-1] for h in ref["layers"]]).astype(np.float32))
+    print("wrote hy_forward_s300.npz")
 
 
 if __name__ == "__main__":

@@ -148,3 +148,58 @@ def test_partials_merge_equals_attend():
     parts = [attention.attend_partials(q, k, v, pb, lo, min(lo + 128, L)) for lo in range(0, L, 128)]
     out = attention.lse_merge(*zip(*parts))
     assert np.abs(out - ref).max() < 1e-5
+
+
+# ---- hybrid-layer glue and the end-to-end forward ----
+
+def test_kc_conv1d():
+    from oracle import glue
+    z = load("kc_conv1d.npz")
+    S, C, K, _ = [int(x) for x in z["params"]]
+    y, st = glue.conv1d_causal(z["in0"].reshape(S, C), z["in1"].reshape(C, K))
+    assert np.array_equal(y.reshape(-1), z["expected"])
+    assert np.array_equal(st, z["in0"].reshape(S, C)[S - (K - 1):])
+
+
+def test_conv1d_segments_carry_state():
+    """Two segments chained through the carried state == one segment (conv1d_causal.wgsl:4-6)."""
+    from oracle import glue
+    z = load("kc_conv1d.npz")
+    S, C, K, _ = [int(x) for x in z["params"]]
+    x, w = z["in0"].reshape(S, C), z["in1"].reshape(C, K)
+    y1, s1 = glue.conv1d_causal(x[:5], w)
+    y2, s2 = glue.conv1d_causal(x[5:], w, s1)
+    assert np.array_equal(np.concatenate([y1, y2]).reshape(-1), z["expected"])
+    y3, s3 = glue.conv1d_causal(x[:1], w)          # shorter than K-1: state keeps zeros
+    assert np.array_equal(s3[:K - 2], np.zeros((K - 2, C), np.float32)) and np.array_equal(s3[-1], x[0])
+
+
+def test_kc_rope_partial():
+    from oracle import glue
+    z = load("kc_rope_partial.npz")
+    S, H, D, R = [int(x) for x in z["params"]]
+    y = glue.rope_partial(z["in0"].reshape(S, H, D), z["in1"].reshape(S, R), z["in2"].reshape(S, R), R)
+    assert np.array_equal(y.reshape(-1), z["expected"])
+
+
+def test_qk_prologue():
+    from oracle import glue
+    z = load("kc_qk_prologue.npz")
+    S, H, D2 = z["qg"].shape
+    D, R = D2 // 2, z["cos"].shape[1]
+    y = glue.qk_norm_rope(z["qg"].reshape(S, -1), H, D, 2 * D, 0, 1.0 + z["w"], z["cos"], z["sin"], R, 1e-6)
+    ok, mad, cos = close(y, z["expected"], tol=1e-6)
+    assert ok, (mad, cos)
+    gate = glue.slice_cols(z["qg"], S * H, D, 2 * D, D).reshape(S, H, D)
+    assert np.array_equal(gate, z["gate"])
+
+
+def test_hybrid_forward_vs_reference():
+    """Restated hybrid forward == the reference's numpy forward on the same seeded weights."""
+    from oracle import hybrid
+    z = load("hy_forward_s300.npz")
+    cfg = hybrid.Cfg()
+    out = hybrid.forward(hybrid.synth_weights(cfg, int(z["seed"])), cfg, z["ids"])
+    assert np.abs(out["logits"][-16:] - z["logits_tail"]).max() < 1e-4
+    assert np.array_equal(out["logits"].argmax(-1), z["argmax"])
+    assert np.abs(np.stack([h[-1] for h in out["layers"]]) - z["last_hidden"]).max() < 1e-4
