@@ -20,6 +20,7 @@ EXPORTS = [
     "bg_deltanet_gbeta", "bg_deltanet_recur", "bg_deltanet_norm_gate", "bg_deltanet_fused",
     "bg_gate_sigmoid", "bg_attention_noalloc", "bg_deltanet_chunked_workspace_size",
     "bg_deltanet_chunked", "bg_qk_norm_rope", "bg_conv1d_causal", "bg_slice_cols",
+    "bg_kv_snapshot_bytes", "bg_kv_snapshot_save", "bg_kv_snapshot_restore",
 ]
 
 
@@ -60,6 +61,9 @@ _SIGS = {
                                   C.POINTER(KVCacheDesc), P]),
     "bg_conv1d_causal": (C.c_int, [P, P, P, U32, U32, U32, U32, P, P, P]),
     "bg_slice_cols": (C.c_int, [P, U32, U32, U32, U32, P, P]),
+    "bg_kv_snapshot_bytes": (SZ, [C.POINTER(KVCacheDesc), U32, U32, U32]),
+    "bg_kv_snapshot_save": (C.c_int, [C.POINTER(KVCacheDesc), U32, U32, U32, U32, U32, P, P]),
+    "bg_kv_snapshot_restore": (C.c_int, [C.POINTER(KVCacheDesc), U32, U32, U32, U32, U32, P, P]),
     "bg_rmsnorm_rope": (C.c_int, [P, U32, U32, U32, P, P, P, F, P, C.POINTER(KVCacheDesc), U32, P]),
     "bg_kv_evict": (C.c_int, [C.POINTER(KVCacheDesc), U32, U32, U32, U32, U32, U32, C.POINTER(U32), P]),
     "bg_kv_ring_evict": (C.c_int, [C.POINTER(KVCacheDesc), U32, U32, U32, C.POINTER(U32)]),

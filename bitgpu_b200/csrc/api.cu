@@ -132,9 +132,80 @@ int run_attention(const bg_attn_params *p, uint32_t batch, const void *q, uint32
   return launch_lse_merge(a.partials, a.nsplit, (uint32_t)rows, p->D, gate, out, out_dtype == BG_DT_F16, st);
 }
 
+// Snapshot regions of one layer, in the reference order (engine.ts:2768-2776): K, V, then the q8
+// block scales of K and V.  Bytes of one cache position of each region, or 0 if absent.
+void snapshot_row_bytes(const bg_kv_cache *kv, uint32_t KV, uint32_t D, uint64_t rb[4]) {
+  const uint64_t es = kv->mode == BG_KV_F32 ? 4 : kv->mode == BG_KV_F16 ? 2 : 1;
+  rb[0] = rb[1] = (uint64_t)KV * D * es;
+  const uint64_t blk = kv->mode == BG_KV_Q8 ? 32 : kv->mode == BG_KV_Q8R ? 128 : 0;
+  rb[2] = rb[3] = blk ? (uint64_t)KV * (D / blk) * 4 : 0;
+}
+
+// Copy logical positions [base, base+count) of sequence `seq` between the cache and a packed
+// snapshot region buffer (to_cache: restore).  A logical range is at most three physical runs of
+// the ring (sinks, head..end of window, wrap), each one contiguous copy per region.
+int snapshot_copy(const bg_kv_cache *kv, uint32_t seq, uint32_t KV, uint32_t D, uint32_t base, uint32_t count,
+                  unsigned char *buf, bool to_cache, cudaStream_t st) {
+  if (!kv || (!buf && count) || !kv_mode_ok(kv->mode) || KV == 0) return BG_EINVAL;
+  if (!d_ok(D)) return BG_EUNSUPPORTED;
+  if (kv->mode == BG_KV_Q8R && D % 128) return BG_EINVAL;
+  const uint64_t cap = kv->window ? (uint64_t)kv->sinks + kv->window : kv->seq_stride;
+  if ((uint64_t)base + count > cap) return BG_EINVAL;
+  void *reg[4] = {kv->K, kv->V, const_cast<float *>(kv->Ks), const_cast<float *>(kv->Vs)};
+  uint64_t rb[4];
+  snapshot_row_bytes(kv, KV, D, rb);
+  for (int r = 0; r < 4; ++r)
+    if (rb[r] && !reg[r]) return BG_EINVAL;
+  const uint32_t head = kv->window ? kv->ring_head % kv->window : 0;
+  uint64_t boff = 0;
+  for (int r = 0; r < 4; ++r) {
+    if (!rb[r]) continue;
+    unsigned char *slab = static_cast<unsigned char *>(reg[r]) + (uint64_t)seq * kv->seq_stride * rb[r];
+    for (uint32_t p = base; p < base + count;) {
+      uint32_t ph = p, run = base + count - p;
+      if (kv->window) {
+        if (p < kv->sinks) {
+          run = min(run, kv->sinks - p);
+        } else {
+          uint32_t rel = head + (p - kv->sinks);
+          if (rel >= kv->window) rel -= kv->window;
+          ph = kv->sinks + rel;
+          run = min(run, kv->window - rel);
+        }
+      }
+      unsigned char *dev = slab + (uint64_t)ph * rb[r];
+      unsigned char *pk = buf + boff + (uint64_t)(p - base) * rb[r];
+      const uint64_t n = (uint64_t)run * rb[r];
+      if (cudaMemcpyAsync(to_cache ? dev : pk, to_cache ? pk : dev, n, cudaMemcpyDefault, st) != cudaSuccess)
+        return BG_ELAUNCH;
+      p += run;
+    }
+    boff += (uint64_t)count * rb[r];
+  }
+  return BG_OK;
+}
+
 }  // namespace
 
 extern "C" {
+
+size_t bg_kv_snapshot_bytes(const bg_kv_cache *kv, uint32_t KV, uint32_t D, uint32_t count) {
+  if (!kv || !kv_mode_ok(kv->mode)) return 0;
+  uint64_t rb[4];
+  snapshot_row_bytes(kv, KV, D, rb);
+  return (size_t)count * (rb[0] + rb[1] + rb[2] + rb[3]);
+}
+
+int bg_kv_snapshot_save(const bg_kv_cache *kv, uint32_t seq, uint32_t KV, uint32_t D, uint32_t base, uint32_t count,
+                        void *dst, bg_stream_t stream) {
+  return snapshot_copy(kv, seq, KV, D, base, count, static_cast<unsigned char *>(dst), false, (cudaStream_t)stream);
+}
+
+int bg_kv_snapshot_restore(const bg_kv_cache *kv, uint32_t seq, uint32_t KV, uint32_t D, uint32_t base,
+                           uint32_t count, const void *src, bg_stream_t stream) {
+  return snapshot_copy(kv, seq, KV, D, base, count, static_cast<unsigned char *>(const_cast<void *>(src)), true,
+                       (cudaStream_t)stream);
+}
 
 const char *bg_strerror(int code) {
   switch (code) {

@@ -147,6 +147,23 @@ int bg_qk_norm_rope(const float *x, uint32_t batch, uint32_t S, uint32_t heads, 
                     const float *sinT, uint32_t rot, uint32_t pos0, float eps, float *y,
                     const bg_kv_cache *kv, bg_stream_t stream);
 
+/* ---- KV snapshot wire format ---------------------------------------------------------------
+ * saveCache / restoreCache of engine.ts:2719-2872 (KvSnapshot, src/types.ts:364-390): one
+ * layer's share of `data` is, for cache positions [base, base+count) in LOGICAL order, the K rows,
+ * then the V rows, then (q8) the K block-scale rows and the V block-scale rows, each row in the
+ * cache's own bytes ([kv_head][D] of f32 / f16 / int8 codes; scales [kv_head][D/32] f32).  On a
+ * ring cache (window > 0) the logical order is gathered from the physical ring (sinks, then the
+ * window from ring_head), so the bytes equal those of the reference's compacted cache; restore
+ * scatters through the same mapping (a restored snapshot is usually written with ring_head = 0).
+ * dst / src may be host (pageable or pinned) or device memory; `seq` selects the sequence of a
+ * batched cache.  The DeltaNet state [H][DK][DV] and the conv left context [K-1][C] that follow
+ * the layers in `data` are plain copies of those buffers. */
+size_t bg_kv_snapshot_bytes(const bg_kv_cache *kv, uint32_t KV, uint32_t D, uint32_t count);
+int bg_kv_snapshot_save(const bg_kv_cache *kv, uint32_t seq, uint32_t KV, uint32_t D, uint32_t base,
+                        uint32_t count, void *dst, bg_stream_t stream);
+int bg_kv_snapshot_restore(const bg_kv_cache *kv, uint32_t seq, uint32_t KV, uint32_t D, uint32_t base,
+                           uint32_t count, const void *src, bg_stream_t stream);
+
 /* ---- hybrid-layer glue --------------------------------------------------------------------
  * bg_conv1d_causal: conv1d_causal.wgsl (engine.ts:1422-1427).  Depthwise causal conv + SiLU over
  * ext = [state_in (K-1 rows, zeros unless load_state); x (S rows)]:
