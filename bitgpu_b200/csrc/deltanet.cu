@@ -12,6 +12,7 @@
 // and add their per-token sums of squares through distributed shared memory.
 #include <cooperative_groups.h>
 #include <math.h>
+#include <stdlib.h>
 
 #include "kv.h"
 
@@ -133,6 +134,128 @@ __global__ void __launch_bounds__(128) deltanet_kernel(DeltaArgs a) {
   }
 }
 
+// Head-per-CTA recurrence for DK = DV = 128 (the 27B's linear layers): 512 threads, warp w owns
+// state rows [32*(w/4), 32*(w/4)+32) of columns [32*(w%4), +32) in registers (lane = column).
+// Every reduction of a token stays inside the CTA -- kv and the output over dk through shared
+// memory, the gated norm's sum of squares over dv with a block reduction -- so no cluster barrier
+// is needed, and the next token's inputs are loaded while the current token is processed.  The
+// gated norm of token t is finished behind token t+1's first barrier (three barriers per token).
+template <bool FUSED>
+__global__ void __launch_bounds__(512) deltanet_head_kernel(DeltaArgs a) {
+  constexpr int DK = 128, DV = 128, RPW = 32;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int cgp = warp & 3, rq = warp >> 2;
+  const uint32_t h = blockIdx.x, hk = h % a.HK;
+  const uint32_t c = cgp * 32 + lane;
+  __shared__ float kn_s[DK], qn_s[DK];
+  __shared__ float red_kv[4][DV], red_o[4][DV];
+  __shared__ float ss_s[4];
+
+  // inputs of token t: warp 0 / 1 carry four k / q values per lane, every thread v[c], the
+  // norm's z[c] (row-quarter-0 warps) and the per-head gate scalars
+  float kq[4], vv, zz = 0.f, ga, gb;
+  auto load_inputs = [&](uint32_t t) {
+    const uint32_t tt = t + a.tOff;
+    const uint64_t base = (uint64_t)tt * a.H + h, basek = (uint64_t)tt * a.HK + hk;
+    if (warp < 2) {
+      const float4 x = *reinterpret_cast<const float4 *>((warp ? a.q : a.k) + basek * DK + lane * 4);
+      kq[0] = x.x; kq[1] = x.y; kq[2] = x.z; kq[3] = x.w;
+    }
+    vv = a.v[base * DV + c];
+    if constexpr (FUSED) {
+      if (rq == 0) zz = a.z[base * DV + c];
+      ga = a.a[base];
+      gb = a.b[base];
+    } else {
+      ga = a.g[base];
+      gb = a.beta[a.betaOff + base];
+    }
+  };
+  if (a.S) load_inputs(0);  // in flight together with the state loads
+
+  float s[RPW];
+  const uint64_t sbase = (uint64_t)h * DK * DV;
+#pragma unroll
+  for (int i = 0; i < RPW; ++i)
+    s[i] = (a.loadState && a.state_in) ? a.state_in[sbase + (uint64_t)(rq * RPW + i) * DV + c] : 0.f;
+  const float qscale = 1.0f / sqrtf((float)DK);
+  const float an = FUSED ? a.a_neg[h] : 0.f, dtb = FUSED ? a.dt_bias[h] : 0.f;
+  const float gam = (FUSED && rq == 0) ? a.gamma[c] : 0.f;
+  float o_prev = 0.f, z_prev = 0.f;
+  uint64_t out_prev = 0;
+
+  for (uint32_t t = 0; t < a.S; ++t) {
+    const uint64_t base = (uint64_t)(t + a.tOff) * a.H + h;
+    // ---- A: l2norm(k), l2norm(q)/sqrt(dk); g, beta ----
+    if (warp < 2) {
+      float ss = kq[0] * kq[0] + kq[1] * kq[1] + kq[2] * kq[2] + kq[3] * kq[3];
+      ss = warp_sum(ss);
+      const float inv = (1.0f / sqrtf(ss + 1e-6f)) * (warp ? qscale : 1.0f);
+      float *dst = (warp ? qn_s : kn_s) + lane * 4;
+      dst[0] = kq[0] * inv; dst[1] = kq[1] * inv; dst[2] = kq[2] * inv; dst[3] = kq[3] * inv;
+    }
+    float gt, bt;
+    if constexpr (FUSED) {
+      gt = expf(an * softplus_stable(ga + dtb));
+      bt = sigmoidf_(gb);
+    } else {
+      gt = expf(ga);
+      bt = gb;
+    }
+    const float v_t = vv, z_t = zz;
+    if (t + 1 < a.S) load_inputs(t + 1);
+    __syncthreads();
+    // the previous token's gated norm: its sum of squares is complete behind this barrier
+    if (FUSED && rq == 0 && t > 0) {
+      const float inv = 1.0f / sqrtf((ss_s[0] + ss_s[1] + ss_s[2] + ss_s[3]) / (float)DV + a.eps);
+      a.y[out_prev] = gam * (o_prev * inv) * (z_prev / (1.0f + expf(-z_prev)));
+    }
+    // ---- B: decay, kv = Kn . S ----
+    float part = 0.f;
+#pragma unroll
+    for (int i = 0; i < RPW; ++i) {
+      s[i] *= gt;
+      part = fmaf(s[i], kn_s[rq * RPW + i], part);
+    }
+    red_kv[rq][c] = part;
+    __syncthreads();
+    // ---- C: delta rule update, o = Qn . S ----
+    const float kvv = (red_kv[0][c] + red_kv[1][c]) + (red_kv[2][c] + red_kv[3][c]);
+    const float delta = (v_t - kvv) * bt;
+    float po = 0.f;
+#pragma unroll
+    for (int i = 0; i < RPW; ++i) {
+      s[i] = fmaf(kn_s[rq * RPW + i], delta, s[i]);
+      po = fmaf(s[i], qn_s[rq * RPW + i], po);
+    }
+    red_o[rq][c] = po;
+    __syncthreads();
+    // ---- D: output column (row-quarter-0 warps) ----
+    if (rq == 0) {
+      const float o = (red_o[0][c] + red_o[1][c]) + (red_o[2][c] + red_o[3][c]);
+      if (a.core) a.core[base * DV + c] = o;
+      if constexpr (FUSED) {
+        const float sq = warp_sum(o * o);
+        if (lane == 0) ss_s[cgp] = sq;
+        o_prev = o;
+        z_prev = z_t;
+        out_prev = base * DV + c;
+      }
+    }
+  }
+  if (FUSED && a.S) {
+    __syncthreads();
+    if (rq == 0) {
+      const float inv = 1.0f / sqrtf((ss_s[0] + ss_s[1] + ss_s[2] + ss_s[3]) / (float)DV + a.eps);
+      a.y[out_prev] = gam * (o_prev * inv) * (z_prev / (1.0f + expf(-z_prev)));
+    }
+  }
+  if (a.state_out) {
+#pragma unroll
+    for (int i = 0; i < RPW; ++i) a.state_out[sbase + (uint64_t)(rq * RPW + i) * DV + c] = s[i];
+  }
+}
+
 __global__ void gbeta_kernel(const float *a, const float *b, const float *an, const float *dt, uint32_t S, uint32_t H,
                              float *out) {
   const uint32_t n = S * H;
@@ -165,10 +288,23 @@ __global__ void gate_sigmoid_kernel(const float *x, const float *g, uint32_t n, 
   if (i < n) y[i] = x[i] / (1.0f + expf(-g[i]));
 }
 
+bool head_legacy() {
+  static const bool v = [] {
+    const char *e = getenv("BGATTN_DN_LEGACY");  // column-group kernel with the cluster norm (A/B)
+    return e && *e == '1';
+  }();
+  return v;
+}
+
 template <int DK>
 int launch_dk(const DeltaArgs &a, cudaStream_t st) {
   const uint32_t ncg = (a.DV + 31) / 32;
   const bool fused = a.z != nullptr;
+  if (DK == 128 && a.DV == 128 && !head_legacy()) {
+    if (fused) deltanet_head_kernel<true><<<a.H, 512, 0, st>>>(a);
+    else deltanet_head_kernel<false><<<a.H, 512, 0, st>>>(a);
+    return cudaGetLastError() == cudaSuccess ? BG_OK : BG_ELAUNCH;
+  }
   if (!fused) {
     deltanet_kernel<DK, false><<<dim3(ncg, a.H), 128, 0, st>>>(a);
     return cudaGetLastError() == cudaSuccess ? BG_OK : BG_ELAUNCH;
