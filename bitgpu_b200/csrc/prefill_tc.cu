@@ -14,7 +14,7 @@
 //     warp 2      TMEM allocator (512 columns: S_a, S_b, O_a, O_b; P_t aliases the first 64
 //                 columns of S_t as packed f16 pairs)
 //     warps 4-7   softmax of tile a, warps 8-11 softmax of tile b: one query row per thread,
-//                 scores read with tcgen05.ld (two passes: row max, then exp2 + pack + store),
+//                 the whole 128-column score row read with tcgen05.ld into registers (one wait),
 //                 online softmax in log2 units.  The running max used for the exponentials is
 //                 raised lazily (only when a row's max grows by more than 2^8), so O is rescaled
 //                 in TMEM rarely; P <= 256 stays well inside f16.
@@ -188,6 +188,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t sQ = smem_u32(sm + PfSmem::Q);
   const uint32_t sKV = smem_u32(sm + PfSmem::KV);
 
+  // Warpgroup 0 (producer, MMA issuer, TMEM owner) runs on 72 registers so the two softmax
+  // warpgroups can hold a whole 128-column score row: 128*72 + 256*216 == 384*168 (launch).
+  if (warp < 4) asm volatile("setmaxnreg.dec.sync.aligned.u32 72;" ::: "memory");
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
@@ -278,6 +281,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = 0; t < 2; ++t) mbar_wait(&o_done[t], (max(j, 1) - 1) & 1);
     }
   } else if (warp >= 4) {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 216;" ::: "memory");
     // ---------------- softmax (one query row per thread) ----------------
     const int t = (warp - 4) >> 2;                 // query tile
     const int row = ((warp & 3) << 5) + lane;      // TMEM lane == tile row
@@ -294,28 +298,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int key0 = j * kKeys;
       // keys of this tile the row may attend: all of them except near the diagonal
       const int nvalid = min(kKeys, max(0, (int)qpos - key0 + 1));
-      // pass 1: row max of the raw scores (two 32-column chunks per TMEM wait)
+      // the whole 128-column score row in registers: one TMEM wait per tile
+      uint32_t r[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(sbase + c * 32, r[c]);
+      tmem_wait_ld();
+      const bool full_row = nvalid >= kKeys;
+      if (!full_row) {  // keys past the diagonal: -inf scores (exp2 -> 0)
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (c * 32 + i >= nvalid) r[c][i] = __float_as_uint(-INFINITY);
+      }
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 4; c += 2) {
-        uint32_t r0[32], r1[32];
-        tmem_ld32(sbase + c * 32, r0);
-        tmem_ld32(sbase + c * 32 + 32, r1);
-        tmem_wait_ld();
-        if (nvalid >= kKeys) {
+      for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            mx = fmax3(mx, __uint_as_float(r0[i]), __uint_as_float(r0[i + 1]));
-            mx = fmax3(mx, __uint_as_float(r1[i]), __uint_as_float(r1[i + 1]));
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            if (c * 32 + i < nvalid) mx = fmaxf(mx, __uint_as_float(r0[i]));
-            if (c * 32 + 32 + i < nvalid) mx = fmaxf(mx, __uint_as_float(r1[i]));
-          }
-        }
-      }
+        for (int i = 0; i < 32; i += 2) mx = fmax3(mx, __uint_as_float(r[c][i]), __uint_as_float(r[c][i + 1]));
       const float mt = mx * sl2;
       if (mt > m_used + kRescaleThreshold) {
         if (j > 0 && m_used > -INFINITY) {
@@ -324,55 +324,38 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t obase = tO[t] | lane_off;
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
-            uint32_t r[32];
-            tmem_ld32(obase + c * 32, r);
+            uint32_t o[32];
+            tmem_ld32(obase + c * 32, o);
             tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
-            tmem_st32(obase + c * 32, r);
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+            tmem_st32(obase + c * 32, o);
           }
           l *= f;
         }
         m_used = mt;
       }
-      // pass 2: p = exp2(s*sl2 - m_used), packed f16 into the first 64 columns of S_t
+      // p = exp2(s*sl2 - m_used), packed f16 into the first 64 columns of S_t
       const float mneg = -m_used;
+      float ls0 = 0.f, ls1 = 0.f;
 #pragma unroll
       for (int c = 0; c < 4; c += 2) {
-        uint32_t r0[32], r1[32];
-        tmem_ld32(sbase + c * 32, r0);
-        tmem_ld32(sbase + c * 32 + 32, r1);
-        tmem_wait_ld();
         uint32_t pk0[16], pk1[16];
-        float ls = 0.f;
-        if (nvalid >= kKeys) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float p0 = ex2_approx(fmaf(__uint_as_float(r0[2 * i]), sl2, mneg));
-            const float p1 = ex2_approx(fmaf(__uint_as_float(r0[2 * i + 1]), sl2, mneg));
-            const float p2 = ex2_approx(fmaf(__uint_as_float(r1[2 * i]), sl2, mneg));
-            const float p3 = ex2_approx(fmaf(__uint_as_float(r1[2 * i + 1]), sl2, mneg));
-            ls += (p0 + p1) + (p2 + p3);
-            pk0[i] = pack_half2(p0, p1);
-            pk1[i] = pack_half2(p2, p3);
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int k0 = c * 32 + 2 * i;
-            const float p0 = k0 < nvalid ? ex2_approx(fmaf(__uint_as_float(r0[2 * i]), sl2, mneg)) : 0.f;
-            const float p1 = k0 + 1 < nvalid ? ex2_approx(fmaf(__uint_as_float(r0[2 * i + 1]), sl2, mneg)) : 0.f;
-            const float p2 = k0 + 32 < nvalid ? ex2_approx(fmaf(__uint_as_float(r1[2 * i]), sl2, mneg)) : 0.f;
-            const float p3 = k0 + 33 < nvalid ? ex2_approx(fmaf(__uint_as_float(r1[2 * i + 1]), sl2, mneg)) : 0.f;
-            ls += (p0 + p1) + (p2 + p3);
-            pk0[i] = pack_half2(p0, p1);
-            pk1[i] = pack_half2(p2, p3);
-          }
+        for (int i = 0; i < 16; ++i) {
+          const float p0 = ex2_approx(fmaf(__uint_as_float(r[c][2 * i]), sl2, mneg));
+          const float p1 = ex2_approx(fmaf(__uint_as_float(r[c][2 * i + 1]), sl2, mneg));
+          const float p2 = ex2_approx(fmaf(__uint_as_float(r[c + 1][2 * i]), sl2, mneg));
+          const float p3 = ex2_approx(fmaf(__uint_as_float(r[c + 1][2 * i + 1]), sl2, mneg));
+          ls0 += p0 + p1;
+          ls1 += p2 + p3;
+          pk0[i] = pack_half2(p0, p1);
+          pk1[i] = pack_half2(p2, p3);
         }
-        l += ls;
         tmem_st16(sbase + c * 16, pk0);
         tmem_st16(sbase + c * 16 + 16, pk1);
       }
+      l += ls0 + ls1;
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&p_full[t]);
