@@ -311,16 +311,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 32; ++i)
             if (c * 32 + i >= nvalid) r[c][i] = __float_as_uint(-INFINITY);
       }
-      float mx = -INFINITY;
+      // eight independent max chains (8 deep each) instead of one 64 deep
+      float mx8[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) mx = fmax3(mx, __uint_as_float(r[c][i]), __uint_as_float(r[c][i + 1]));
+        for (int i = 0; i < 32; i += 2) {
+          const int k = (c * 16 + i / 2) & 7;
+          mx8[k] = fmax3(mx8[k], __uint_as_float(r[c][i]), __uint_as_float(r[c][i + 1]));
+        }
+      const float mx = fmaxf(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], fmaxf(mx8[5], fmaxf(mx8[6], mx8[7]))));
       const float mt = mx * sl2;
-      if (mt > m_used + kRescaleThreshold) {
-        if (j > 0 && m_used > -INFINITY) {
+      // lazy rescale; the TMEM round trip is .sync.aligned, so the branch is taken by the whole
+      // warp when any of its rows moved, and rows that did not move use the factor 1
+      const bool need = mt > m_used + kRescaleThreshold;
+      if (__any_sync(0xffffffffu, need)) {
+        if (j > 0) {
           // PV_t(j-1) has completed: the commit we waited on (after S_t(j)) covers it.
-          const float f = ex2_approx(m_used - mt);
+          const float f = (need && m_used > -INFINITY) ? ex2_approx(m_used - mt) : 1.0f;
           const uint32_t obase = tO[t] | lane_off;
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
@@ -333,10 +343,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           l *= f;
         }
-        m_used = mt;
+        if (need) m_used = mt;
       }
-      // p = exp2(s*sl2 - m_used), packed f16 into the first 64 columns of S_t
       const float mneg = -m_used;
+      // p = exp2(s*sl2 - m_used), packed f16 into the first 64 columns of S_t (masked scores hold
+      // -inf -> 0).  Moving a share of these exponentials to the FMA pipe with a polynomial was
+      // measured slower (one in eight: -3 %, one in four: -12 %): the softmax is bound by its
+      // instruction count and latency more than by MUFU throughput.
       float ls0 = 0.f, ls1 = 0.f;
 #pragma unroll
       for (int c = 0; c < 4; c += 2) {

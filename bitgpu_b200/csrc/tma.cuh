@@ -11,7 +11,7 @@
 
 namespace bg {
 
-constexpr uint32_t kSpinLimit = 1u << 24;
+constexpr uint32_t kSpinLimit = 1u << 20;  // far above any legitimate wait; a fault fails fast
 
 // Per-translation-unit timeout flag (no relocatable device code): each .cu that includes this
 // header exposes a host poll function that reads and clears its copy; bg_device_status polls all.
