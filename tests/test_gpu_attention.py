@@ -222,3 +222,36 @@ def test_roll_tensor_core_vs_generic(ops, mode, S, ring_head):
     err = (a - b).abs().max().item()
     assert err < 1e-3, err
     assert lib().bg_device_status(None) == 0
+
+
+@pytest.mark.parametrize("mode", ["f16", "q8"])
+@pytest.mark.parametrize("H,KV,S", [(16, 4, 1), (12, 2, 1), (12, 6, 1), (9, 3, 1), (32, 8, 3)])
+def test_roll_head_groups(ops, mode, H, KV, S):
+    """Rope-at-read kernels across kv-head grouping: 4 and 2 heads per CTA (KV = 4, 2, 6), no
+    grouping (KV = 3: the one-head-per-CTA kernel) and a GQA group wider than 8 rows (H32 KV8,
+    S = 3: the two-column-tile kernel), on a wrapped ring, vs the CUDA-core kernel and the oracle."""
+    from bitgpu_b200._lib import lib
+    B, D, SINKS, W = 2, 128, 4, 1000
+    rng = np.random.default_rng(H * 100 + KV * 10 + S)
+    cache = ops.KVCache(B, 0, KV, D, mode=mode, sinks=SINKS, window=W)
+    cache.ring_head = 321
+    L = SINKS + W - 7
+    Kraw, Vraw = rand(rng, B, L, KV, D), rand(rng, B, L, KV, D)
+    Kd, Vd = fill_cache(cache, Kraw, Vraw)
+    c, s_ = OR.synth_rope(D, SINKS + W, 1e6, "yarn", 4.0, 8192)
+    cos_t, sin_t = torch.from_numpy(c).cuda(), torch.from_numpy(s_).cuda()
+    q = rand(rng, B, S, H, D)
+    a = ops.attention(torch.from_numpy(q).cuda(), cache, L - S, cos_t=cos_t, sin_t=sin_t)
+    prev = lib().bg_force_generic(1)
+    try:
+        g = ops.attention(torch.from_numpy(q).cuda(), cache, L - S, cos_t=cos_t, sin_t=sin_t)
+    finally:
+        lib().bg_force_generic(prev)
+    assert (a - g).abs().max().item() < 1e-3
+    an = a.cpu().numpy()
+    for b in range(B):
+        exp = OA.attend(q[b], OA.rotate_keys_at_read(Kd[b], c, s_), Vd[b], L - S)
+        ok, mad, cs = gate_ok(an[b], exp, tol=TOL)
+        assert ok, (mode, H, KV, S, b, mad, cs)
+    assert lib().bg_device_status(None) == 0
+
