@@ -256,6 +256,137 @@ __global__ void __launch_bounds__(512) deltanet_head_kernel(DeltaArgs a) {
   }
 }
 
+// Decode-length variant (a few tokens per call) of the head-per-CTA recurrence: thread = warp w's
+// rows [8w, 8w+8) x lane's columns [4*lane, 4*lane+4), so the state moves as eight float4 loads
+// and stores per thread (the scalar layout above issues 32 of each and is load/store-queue bound
+// when one launch is one token).  Reductions over dk sum 16 row-group partials per column from
+// shared memory; warp 0 holds all 128 columns of the output and finishes the gated norm alone.
+template <bool FUSED>
+__global__ void __launch_bounds__(512) deltanet_head_vec_kernel(DeltaArgs a) {
+  constexpr int DK = 128, DV = 128, R = 8;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t h = blockIdx.x, hk = h % a.HK;
+  const int c0 = lane * 4, r0 = warp * R;
+  __shared__ float kn_s[DK], qn_s[DK];
+  __shared__ __align__(16) float red_kv[16][DV], red_o[16][DV];
+
+  float kq[4], ga, gb;
+  float4 vv, zz = make_float4(0.f, 0.f, 0.f, 0.f);
+  auto load_inputs = [&](uint32_t t) {
+    const uint32_t tt = t + a.tOff;
+    const uint64_t base = (uint64_t)tt * a.H + h, basek = (uint64_t)tt * a.HK + hk;
+    if (warp < 2) {
+      const float4 x = *reinterpret_cast<const float4 *>((warp ? a.q : a.k) + basek * DK + lane * 4);
+      kq[0] = x.x; kq[1] = x.y; kq[2] = x.z; kq[3] = x.w;
+    }
+    vv = *reinterpret_cast<const float4 *>(a.v + base * DV + c0);
+    if constexpr (FUSED) {
+      if (warp == 0) zz = *reinterpret_cast<const float4 *>(a.z + base * DV + c0);
+      ga = a.a[base];
+      gb = a.b[base];
+    } else {
+      ga = a.g[base];
+      gb = a.beta[a.betaOff + base];
+    }
+  };
+  if (a.S) load_inputs(0);
+
+  float s[R][4];
+  const uint64_t sbase = (uint64_t)h * DK * DV;
+#pragma unroll
+  for (int i = 0; i < R; ++i) {
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (a.loadState && a.state_in)
+      x = *reinterpret_cast<const float4 *>(a.state_in + sbase + (uint64_t)(r0 + i) * DV + c0);
+    s[i][0] = x.x; s[i][1] = x.y; s[i][2] = x.z; s[i][3] = x.w;
+  }
+  const float qscale = 1.0f / sqrtf((float)DK);
+  const float an = FUSED ? a.a_neg[h] : 0.f, dtb = FUSED ? a.dt_bias[h] : 0.f;
+  float4 gam = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (FUSED && warp == 0) gam = *reinterpret_cast<const float4 *>(a.gamma + c0);
+
+  for (uint32_t t = 0; t < a.S; ++t) {
+    const uint64_t base = (uint64_t)(t + a.tOff) * a.H + h;
+    if (warp < 2) {  // l2norm(k), l2norm(q)/sqrt(dk)
+      float ss = kq[0] * kq[0] + kq[1] * kq[1] + kq[2] * kq[2] + kq[3] * kq[3];
+      ss = warp_sum(ss);
+      const float inv = (1.0f / sqrtf(ss + 1e-6f)) * (warp ? qscale : 1.0f);
+      float *dst = (warp ? qn_s : kn_s) + lane * 4;
+      dst[0] = kq[0] * inv; dst[1] = kq[1] * inv; dst[2] = kq[2] * inv; dst[3] = kq[3] * inv;
+    }
+    float gt, bt;
+    if constexpr (FUSED) {
+      gt = expf(an * softplus_stable(ga + dtb));
+      bt = sigmoidf_(gb);
+    } else {
+      gt = expf(ga);
+      bt = gb;
+    }
+    const float vt[4] = {vv.x, vv.y, vv.z, vv.w};
+    const float zt[4] = {zz.x, zz.y, zz.z, zz.w};
+    if (t + 1 < a.S) load_inputs(t + 1);
+    __syncthreads();
+    float kn[R], qn[R];
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+      kn[i] = kn_s[r0 + i];
+      qn[i] = qn_s[r0 + i];
+    }
+    float part[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < R; ++i)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        s[i][c] *= gt;
+        part[c] = fmaf(s[i][c], kn[i], part[c]);
+      }
+    *reinterpret_cast<float4 *>(&red_kv[warp][c0]) = make_float4(part[0], part[1], part[2], part[3]);
+    __syncthreads();
+    float kvv[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int w = 0; w < 16; ++w) {
+      const float4 x = *reinterpret_cast<const float4 *>(&red_kv[w][c0]);
+      kvv[0] += x.x; kvv[1] += x.y; kvv[2] += x.z; kvv[3] += x.w;
+    }
+    float po[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const float delta = (vt[c] - kvv[c]) * bt;
+#pragma unroll
+      for (int i = 0; i < R; ++i) {
+        s[i][c] = fmaf(kn[i], delta, s[i][c]);
+        po[c] = fmaf(s[i][c], qn[i], po[c]);
+      }
+    }
+    *reinterpret_cast<float4 *>(&red_o[warp][c0]) = make_float4(po[0], po[1], po[2], po[3]);
+    __syncthreads();
+    if (warp == 0) {
+      float o[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int w = 0; w < 16; ++w) {
+        const float4 x = *reinterpret_cast<const float4 *>(&red_o[w][c0]);
+        o[0] += x.x; o[1] += x.y; o[2] += x.z; o[3] += x.w;
+      }
+      if (a.core) *reinterpret_cast<float4 *>(a.core + base * DV + c0) = make_float4(o[0], o[1], o[2], o[3]);
+      if constexpr (FUSED) {
+        const float sq = warp_sum(o[0] * o[0] + o[1] * o[1] + o[2] * o[2] + o[3] * o[3]);
+        const float inv = 1.0f / sqrtf(sq / (float)DV + a.eps);
+        const float g4[4] = {gam.x, gam.y, gam.z, gam.w};
+        float y[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) y[c] = g4[c] * (o[c] * inv) * (zt[c] / (1.0f + expf(-zt[c])));
+        *reinterpret_cast<float4 *>(a.y + base * DV + c0) = make_float4(y[0], y[1], y[2], y[3]);
+      }
+    }
+  }
+  if (a.state_out) {
+#pragma unroll
+    for (int i = 0; i < R; ++i)
+      *reinterpret_cast<float4 *>(a.state_out + sbase + (uint64_t)(r0 + i) * DV + c0) =
+          make_float4(s[i][0], s[i][1], s[i][2], s[i][3]);
+  }
+}
+
 __global__ void gbeta_kernel(const float *a, const float *b, const float *an, const float *dt, uint32_t S, uint32_t H,
                              float *out) {
   const uint32_t n = S * H;
@@ -288,6 +419,16 @@ __global__ void gate_sigmoid_kernel(const float *x, const float *g, uint32_t n, 
   if (i < n) y[i] = x[i] / (1.0f + expf(-g[i]));
 }
 
+constexpr uint32_t kVecMaxTokens = 16;
+
+// the vector layout reads state, q/k, v, z, gamma and writes state, core, y as float4
+bool aligned16(const DeltaArgs &a) {
+  const void *ps[] = {a.state_in, a.state_out, a.q, a.k, a.v, a.z, a.gamma, a.core, a.y};
+  for (const void *x : ps)
+    if (reinterpret_cast<uintptr_t>(x) % 16) return false;
+  return true;
+}
+
 bool head_legacy() {
   static const bool v = [] {
     const char *e = getenv("BGATTN_DN_LEGACY");  // column-group kernel with the cluster norm (A/B)
@@ -301,7 +442,12 @@ int launch_dk(const DeltaArgs &a, cudaStream_t st) {
   const uint32_t ncg = (a.DV + 31) / 32;
   const bool fused = a.z != nullptr;
   if (DK == 128 && a.DV == 128 && !head_legacy()) {
-    if (fused) deltanet_head_kernel<true><<<a.H, 512, 0, st>>>(a);
+    // short calls (decode) take the vector layout; long recurrent runs keep the scalar one, whose
+    // per-token reductions are four partials instead of sixteen
+    const bool vec = a.S <= kVecMaxTokens && aligned16(a);
+    if (vec && fused) deltanet_head_vec_kernel<true><<<a.H, 512, 0, st>>>(a);
+    else if (vec) deltanet_head_vec_kernel<false><<<a.H, 512, 0, st>>>(a);
+    else if (fused) deltanet_head_kernel<true><<<a.H, 512, 0, st>>>(a);
     else deltanet_head_kernel<false><<<a.H, 512, 0, st>>>(a);
     return cudaGetLastError() == cudaSuccess ? BG_OK : BG_ELAUNCH;
   }
