@@ -474,12 +474,6 @@ __global__ void __launch_bounds__(RCfg<MODE, HPC>::THREADS, 1)
     // column for up to 32 slots, and two independent score chains in flight.
     auto step = [&](auto nsub_c, const uint32_t (&cu)[2], const Tile (&tl)[2], const int (&st)[2]) {
       constexpr int NSUB = decltype(nsub_c)::value;
-#ifdef BG_EXP_NOCOMPUTE
-      __syncwarp();
-      if (lane == 0)
-        for (int u = 0; u < NSUB; ++u) mbar_arrive(&empty[st[u]]);
-      return;
-#endif
       float acc[NSUB][4];
 #pragma unroll
       for (int u = 0; u < NSUB; ++u)
