@@ -25,7 +25,10 @@ import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
-os.environ["NCCL_DEBUG"] = os.environ.get("BENCH_NCCL_DEBUG", "WARN")  # stdout carries only the JSON line
+# NCCL's INIT lines (rank count, transport, NVLS) go to stderr: stdout carries only the JSON line
+os.environ.setdefault("NCCL_DEBUG", "INFO")
+os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
 
 # config 2; manifest models/bonsai-8b-gguf: heads 32, kv_heads 8, head_dim 128
 B, L, H, KV, D = 64, 32768, 32, 8, 128
@@ -160,12 +163,36 @@ def time_steps(torch, fn, steps, warmup, barrier):
     return e0.elapsed_time(e1) / steps  # ms per step
 
 
+def host_threads():
+    """Use every host core for the CPU arms (torch.distributed.run sets OMP_NUM_THREADS=1 for
+    each rank, which would otherwise leave the numpy reference on one BLAS thread).  Returns
+    (threads used, physical cores, logical cores)."""
+    logical = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    try:
+        import psutil
+        physical = psutil.cpu_count(logical=False) or logical
+    except Exception:  # noqa: BLE001
+        physical = logical
+    try:
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(limits=physical)
+    except Exception:  # noqa: BLE001
+        pass
+    try:
+        from threadpoolctl import threadpool_info
+        used = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+    except Exception:  # noqa: BLE001
+        used = physical
+    return used, physical, logical
+
+
 def cpu_baseline(mode, seconds, seed=0):
     """The oracle (numpy port of the reference attention, f32 math over the storage codec's
     values) on one sequence x one layer of config 2, repeated for ~`seconds`."""
     import numpy as np
     from oracle import attention as OA
     from oracle import kvcodec
+    host_threads()
     rng = np.random.default_rng(seed)
     kr = rng.standard_normal((L, KV, D), dtype=np.float32)
     vr = rng.standard_normal((L, KV, D), dtype=np.float32)
@@ -181,13 +208,10 @@ def cpu_baseline(mode, seconds, seed=0):
         if el >= seconds:
             break
     per = el / n
-    try:
-        from threadpoolctl import threadpool_info
-        cores = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
-    except Exception:
-        cores = os.cpu_count()
+    cores, physical, logical = host_threads()
     gbs = alg_bytes(mode, batch=1) / per / 1e9
-    return {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "physical_cores": physical,
+            "logical_cores": logical, "kind": "port",
             "sample": f"oracle numpy attention, 1 sequence x 1 layer of config 2 ({mode} cache, ctx {L}), "
                       f"{n} reps in {el:.1f} s; same algorithmic bytes per sequence as the GPU metric",
             "ms_per_sequence": round(per * 1e3, 3)}
@@ -200,6 +224,7 @@ def run_reference(args):
     import numpy as np
     from oracle import attention as OA
     from oracle import kvcodec
+    cores, physical, logical = host_threads()
     rng = np.random.default_rng(0)
     kr = rng.standard_normal((L, KV, D), dtype=np.float32)
     vr = rng.standard_normal((L, KV, D), dtype=np.float32)
@@ -212,19 +237,15 @@ def run_reference(args):
     for _ in range(args.steps):
         OA.attend(q, kd, vd, L - 1)
     per = (time.perf_counter() - t0) / args.steps
-    try:
-        from threadpoolctl import threadpool_info
-        cores = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
-    except Exception:
-        cores = os.cpu_count()
     val = alg_bytes("f16", batch=1) / per / 1e9
     sample = (f"one sequence x one layer of config 2 per step (f16 cache, ctx {L}); the reference's CPU attention "
               f"path restated in numpy (oracle/attention.py), {cores} BLAS threads")
     line = {"metric": METRIC, "value": round(val, 3), "unit": "GB/s", "impl": "reference", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per * 1e3, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1), seed 0",
-            "config": CONFIG,
-            "cpu_baseline": {"value": round(val, 3), "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample},
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic N(0,1), seed 0",
+            "config": dict(CONFIG, global_batch_per_gpu=B, kv_mode="f16"),
+            "cpu_baseline": {"value": round(val, 3), "unit": "GB/s", "cores": cores, "physical_cores": physical,
+                             "logical_cores": logical, "kind": "port", "sample": sample},
             "e2e": {"value": round(val, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 

@@ -20,7 +20,8 @@ EXPORTS = [
     "bg_deltanet_gbeta", "bg_deltanet_recur", "bg_deltanet_norm_gate", "bg_deltanet_fused",
     "bg_gate_sigmoid", "bg_attention_noalloc", "bg_deltanet_chunked_workspace_size",
     "bg_deltanet_chunked", "bg_qk_norm_rope", "bg_conv1d_causal", "bg_slice_cols",
-    "bg_kv_snapshot_bytes", "bg_kv_snapshot_save", "bg_kv_snapshot_restore",
+    "bg_kv_snapshot_bytes", "bg_kv_snapshot_save", "bg_kv_snapshot_restore", "bg_attention_noalloc_limit",
+    "bg_selftest_wait_expiry",
 ]
 
 
@@ -74,6 +75,8 @@ _SIGS = {
     "bg_gate_sigmoid": (C.c_int, [P, P, U32, P, P]),
     "bg_deltanet_chunked_workspace_size": (SZ, [U32, U32, U32, U32]),
     "bg_deltanet_chunked": (C.c_int, [U32, U32, U32, U32, U32, P, P, P, P, P, P, P, P, P, F, P, P, P, P, P, SZ, P]),
+    "bg_attention_noalloc_limit": (SZ, []),
+    "bg_selftest_wait_expiry": (C.c_int, [U32, P]),
     "bg_attention_noalloc": (C.c_int, [C.POINTER(AttnParams), U32, P, U32, C.POINTER(KVCacheDesc), P, P, F, P, P,
                                        U32, P]),
 }

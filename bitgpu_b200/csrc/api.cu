@@ -232,6 +232,7 @@ int bg_device_status(bg_stream_t stream) {
   int e = poll_device_error_attn_tc();
   if (!e) e = poll_device_error_attn_roll();
   if (!e) e = poll_device_error_prefill();
+  if (!e) e = poll_device_error_selftest();
   return e ? (e < 0 ? e : BG_ELAUNCH) : BG_OK;
 }
 

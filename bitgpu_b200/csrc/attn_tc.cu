@@ -605,7 +605,7 @@ __global__ void __launch_bounds__(160, (MODE == BG_KV_Q8 && NT == 1 && D == 128 
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           const int d = MODE == BG_KV_F16 ? mt * 16 + (lane >> 2) + 8 * hh : mt * 16 + 2 * (lane >> 2) + hh;
-          mine[n * (D + 2) + d] = oacc[nt][mt][2 * hh + j];
+          mine[n * (D + 2) + d] = ok ? oacc[nt][mt][2 * hh + j] : 0.f;  // timed out: an empty partial
         }
       }
     }
@@ -627,7 +627,7 @@ __global__ void __launch_bounds__(160, (MODE == BG_KV_Q8 && NT == 1 && D == 128 
     const uint32_t qi = n / p.G, h = kvh * p.G + n % p.G;
     const uint64_t grow = ((uint64_t)b * p.S + qi) * p.H + h;
     if (p.out) {  // single split: final output
-      float v = o / L;
+      float v = L > 0.f ? o / L : 0.f;  // L == 0 only after a timed-out wait (BG_ETIMEOUT)
       if (p.gate) v = v / (1.0f + expf(-p.gate[grow * D + d]));
       if (p.out_f16) static_cast<__half *>(p.out)[grow * D + d] = __float2half_rn(v);
       else static_cast<float *>(p.out)[grow * D + d] = v;

@@ -8,39 +8,30 @@
 // not call cudaMalloc, which can synchronise the device.  For them this entry point keeps its
 // scratch in a fixed array compiled into the library (kNoAllocScratchBytes per GPU, resident on
 // every GPU that loads the library until the process exits) and allocates nothing at all.
-#include <mutex>
-
 #include "attn.h"
 
 namespace {
 
-constexpr size_t kNoAllocScratchBytes = 8u << 20;  // 8 MiB per device
+constexpr size_t kNoAllocScratchBytes = BG_NOALLOC_SCRATCH_BYTES;  // 8 MiB per device
 
 // The scratch itself.  In host code this name is only a host-side stand-in for the symbol:
 // kernels must be given the device address from cudaGetSymbolAddress, never &g_noalloc_scratch.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_mu;
-void *g_scratch_ptr[kMaxDevices] = {};
-
-// Device address of the scratch on the current device, looked up once per device (with that
-// device current) and cached.  Returns nullptr on failure.
+// Device address of the scratch in the current context, looked up on every call (a cheap host-side
+// table lookup).  Not caching it keeps the address right after cudaDeviceReset, which recreates
+// the context and may place the module's symbols elsewhere.  Returns nullptr on failure.
 void *scratch_for_current_device() {
-  int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
-  std::lock_guard<std::mutex> lk(g_mu);
-  if (!g_scratch_ptr[dev]) {
-    void *p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return nullptr;
-    g_scratch_ptr[dev] = p;
-  }
-  return g_scratch_ptr[dev];
+  void *p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess) return nullptr;
+  return p;
 }
 
 }  // namespace
 
 extern "C" {
+
+size_t bg_attention_noalloc_limit(void) { return kNoAllocScratchBytes; }
 
 int bg_attention_noalloc(const bg_attn_params *p, uint32_t batch, const void *q, uint32_t q_dtype,
                          const bg_kv_cache *kv, const float *cosT, const float *sinT, float scale, const float *gate,

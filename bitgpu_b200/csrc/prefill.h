@@ -17,5 +17,6 @@ struct PrefillArgs {
 bool prefill_tc_supported(int mode, uint32_t D, uint32_t S, int q_f16, bool roll, bool ring);
 int launch_prefill_tc(const PrefillArgs &a, cudaStream_t st);
 int poll_device_error_prefill();
+int poll_device_error_selftest();
 
 }  // namespace bg

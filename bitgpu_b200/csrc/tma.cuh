@@ -43,12 +43,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait for the phase with the given parity; false (and the device error flag set) on expiry.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i)
+// Bounded wait for the phase with the given parity; false (and the device error flag set) after
+// `limit` polls.
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t *bar, uint32_t parity, uint32_t limit) {
+  for (uint32_t i = 0; i < limit; ++i)
     if (mbar_try_wait(bar, parity)) return true;
   atomicExch(&g_device_error, BG_ETIMEOUT);
   return false;
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+  return mbar_wait_limit(bar, parity, kSpinLimit);
 }
 
 // Whole-warp form: every lane polls, then the warp reconverges (__all_sync) before the

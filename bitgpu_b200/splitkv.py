@@ -21,6 +21,13 @@ import torch
 import torch.distributed as dist
 
 
+class PeerFailure(RuntimeError):
+    """The exchange of one step did not complete: a rank left (raised, exited, or never joined
+    the step) and the collective ended with an error or ran into the process group's timeout.
+    The surviving ranks raise this instead of waiting forever; the stream's output for that step
+    does not exist."""
+
+
 def split_bounds(L, world):
     """Contiguous, near-equal slices of ``L`` positions over ``world`` ranks:
     ``[(lo, hi), ...]``; the first ``L % world`` ranks take one extra position."""
@@ -66,6 +73,9 @@ class SplitKVDecoder:
         else:
             rows, w = part.shape
             flat = torch.empty((self.world * rows, w), dtype=part.dtype, device=part.device)
-            dist.all_gather_into_tensor(flat, part.contiguous(), group=self.group)
+            try:
+                dist.all_gather_into_tensor(flat, part.contiguous(), group=self.group)
+            except (RuntimeError, dist.DistError) as e:  # peer gone or timed out
+                raise PeerFailure(f"split-KV exchange failed on rank {self.rank} of {self.world}: {e}") from e
             gathered = flat.view(self.world, rows, w)
         return self.merge_fn(gathered, (B, S, H, D), gate)

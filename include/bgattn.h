@@ -66,6 +66,12 @@ int bg_version(void);
  * these kernels is bounded; on expiry the kernel records the timeout and returns instead of
  * hanging (the engine's device-lost path, engine.ts:400-409, is the reference counterpart). */
 int bg_device_status(bg_stream_t stream);
+/* Self-test of the bounded device waits (no reference counterpart: the reference's device-lost
+ * path, engine.ts:400-409, is driven by the browser).  Launches one CTA that waits on an
+ * mbarrier nothing ever arrives on, giving up after `polls` polls (1 .. 2^20) exactly as every
+ * kernel of this library gives up after its own limit: the kernel records BG_ETIMEOUT and
+ * returns, the context stays usable, and bg_device_status(stream) then reports BG_ETIMEOUT. */
+int bg_selftest_wait_expiry(uint32_t polls, bg_stream_t stream);
 /* Route every attention call through the CUDA-core kernel instead of the tensor-core one (the
  * reference's forceNoSubgroups option, src/types.ts / engine.ts:282, which forces the _wg
  * fallback kernels).  Process-wide; returns the previous setting.  For A/B checks only. */
@@ -92,13 +98,17 @@ int bg_attention(const bg_attn_params *p, uint32_t batch, const void *q, uint32_
  * No counterpart in the reference (its kernels take every buffer from the engine).  Some hosts
  * cannot hand over a scratch buffer: the engine's device memory may all belong to another
  * allocator with none exposed across the binding, or the token loop may not call cudaMalloc
- * (which can synchronise the device).  This variant takes no workspace: it uses a fixed 8 MiB
- * scratch array compiled into the library, held on every GPU that loads the library until the
- * process exits.  Same arguments and results as bg_attention minus the workspace; returns
- * BG_ENOMEM when bg_attention_workspace_size(p, batch) exceeds 8 MiB.  The first call on a device
- * looks up the array's device address with that device current (make that first call before
- * any stream capture).  All calls share the one array: calls that overlap on the GPU (different
- * streams, or several host threads) race on it and must be serialised by the caller. */
+ * (which can synchronise the device).  This variant takes no workspace: it uses a fixed
+ * BG_NOALLOC_SCRATCH_BYTES (8 MiB) scratch array compiled into the library, held on every GPU
+ * that loads the library until the process exits.  Same arguments and results as bg_attention
+ * minus the workspace; returns BG_ENOMEM when bg_attention_workspace_size(p, batch) exceeds the
+ * limit (bg_attention_noalloc_limit() reports it).  Every call looks up the array's device
+ * address in the current context (so it stays right after cudaDeviceReset); make the first call
+ * on a device before any stream capture.  All calls share the one array: calls that overlap on
+ * the GPU (different streams, or several host threads) race on it and must be serialised by the
+ * caller. */
+#define BG_NOALLOC_SCRATCH_BYTES ((size_t)8 << 20)
+size_t bg_attention_noalloc_limit(void);
 int bg_attention_noalloc(const bg_attn_params *p, uint32_t batch, const void *q, uint32_t q_dtype,
                          const bg_kv_cache *kv, const float *cosT, const float *sinT, float scale,
                          const float *gate, void *out, uint32_t out_dtype, bg_stream_t stream);

@@ -110,3 +110,27 @@ def lse_merge(ms, ls, os_, gate=None):
     if gate is not None:
         O = (O / (F32(1.0) + np.exp(-np.asarray(gate, F32)))).astype(F32)
     return O
+
+
+def attend_rows(q_rows, positions, K, V, scale=None, gate=None):
+    """Selected query rows only: ``q_rows[n, D]`` (one head) at absolute positions
+    ``positions[n]``, over one kv head's ``K, V[L, D]`` (float32 values).  Row ``i`` attends
+    cache positions ``0 .. positions[i]`` -- the same causal rule and softmax as ``attend``
+    (``shaders/attention_sg.wgsl:21-44``), restricted to the rows asked for so that parity at
+    full prefill sizes (8192 rows x 8192 positions) stays a few matrix products."""
+    q = np.asarray(q_rows, F32)
+    D = q.shape[-1]
+    pos = np.asarray(positions)
+    Lmax = int(pos.max()) + 1
+    Kf = np.asarray(K[:Lmax], F32)
+    Vf = np.asarray(V[:Lmax], F32)
+    sc_ = default_scale(D) if scale is None else F32(scale)
+    sc = (q @ Kf.T) * sc_
+    sc = np.where(np.arange(Lmax)[None, :] <= pos[:, None], sc, F32(-1e30)).astype(F32)
+    sc = sc - sc.max(-1, keepdims=True)
+    p = np.exp(sc)
+    p /= p.sum(-1, keepdims=True)
+    out = (p @ Vf).astype(F32)
+    if gate is not None:
+        out = (out / (F32(1.0) + np.exp(-np.asarray(gate, F32)))).astype(F32)
+    return out

@@ -12,7 +12,8 @@ chunked) and for gated / plain causal attention at head_dim 256 and 128 (through
 ``_full_attention`` with an identity hidden state and identity output projection, so the
 expected array is exactly the gated attention output the kernels must produce); (3) runs the
 reference's q/k prologue functions and its whole hybrid ``forward`` on seeded dense weights
-(``oracle.hybrid.synth_weights``) for the end-to-end check.
+(``oracle.hybrid.synth_weights``) for the end-to-end check; (4) copies the reference's own
+fixture of its synthetic 1-bit hybrid model (``test-fixtures/forward-synth-qwen35``).
 """
 import glob
 import json
@@ -121,6 +122,21 @@ def main(ref):
                         last_hidden=np.stack([h[-1] for h in ref["layers"]]).astype(np.float32))
     print("wrote hy_forward_s300.npz")
 
+    # (2e) the reference's own end-to-end fixture for its synthetic 1-bit hybrid model
+    # (test-fixtures/forward-synth-qwen35, written by tools/gen-synth-qwen35.py with the reference's
+    # numpy forward): copied byte for byte.  oracle.synth_qwen35 regenerates the weights.
+    fx = os.path.join(os.path.dirname(tools), "test-fixtures", "forward-synth-qwen35")
+    prm = json.load(open(os.path.join(fx, "params.json")))
+    S, Hd, V = prm["S"], prm["hidden"], prm["vocab"]
+    rd = lambda n, *shape: np.fromfile(os.path.join(fx, n), np.float32).reshape(shape)
+    np.savez_compressed(os.path.join(HERE, "synth_qwen35_fixture.npz"),
+                        ids=np.fromfile(os.path.join(fx, "ids.i32.bin"), np.int32),
+                        logits=rd("logits.bin", S, V), layer0=rd("layer0.bin", S, Hd),
+                        embed_tail=rd("embed.bin", S, Hd)[-32:], argmax_last=np.int64(prm["argmax_last"]))
+    print("wrote synth_qwen35_fixture.npz")
+
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py <path of the bitgpu source tree>")
+    main(sys.argv[1])

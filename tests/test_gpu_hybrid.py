@@ -98,3 +98,22 @@ def test_hybrid_q8_cache(case):
     lg = logits.cpu().numpy()
     assert (lg.argmax(-1) == z["argmax"]).mean() >= 0.97
     assert np.abs(lg[-16:] - z["logits_tail"]).max() < 0.05 * max(1.0, np.abs(z["logits_tail"]).max())
+
+
+def test_synth_qwen35_reference_fixture():
+    """The reference's own end-to-end fixture (test-fixtures/forward-synth-qwen35: its synthetic
+    1-bit hybrid model, seed 1, through its numpy forward): the 4-layer forward with this
+    library's token-mixer kernels on the same dequantised weights gives the fixture's logits
+    (max|d| < 5e-3, cos > 0.9999) and its greedy token argmax_last = 201
+    (scripts/verify-hybrid.mjs:146-161)."""
+    from oracle import synth_qwen35 as SQ
+    z = np.load(os.path.join(GOLDEN, "synth_qwen35_fixture.npz"))
+    cfg, W = SQ.synth_weights()
+    logits, _ = Model(W, cfg)(z["ids"])
+    lg = logits.cpu().numpy()
+    ref = z["logits"]
+    err = float(np.abs(lg - ref).max())
+    cos = float((lg * ref).sum() / (np.linalg.norm(lg) * np.linalg.norm(ref)))
+    assert err < 5e-3 and cos > 0.9999, (err, cos)
+    assert int(lg[-1].argmax()) == int(z["argmax_last"]) == 201
+    assert (lg.argmax(-1) == ref.argmax(-1)).all()

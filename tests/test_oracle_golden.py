@@ -203,3 +203,20 @@ def test_hybrid_forward_vs_reference():
     assert np.abs(out["logits"][-16:] - z["logits_tail"]).max() < 1e-4
     assert np.array_equal(out["logits"].argmax(-1), z["argmax"])
     assert np.abs(np.stack([h[-1] for h in out["layers"]]) - z["last_hidden"]).max() < 1e-4
+
+
+def test_synth_qwen35_weights_and_forward_match_reference_fixture():
+    """oracle.synth_qwen35 redraws the reference's synthetic 1-bit hybrid model
+    (tools/gen-synth-qwen35.py, seed 1): its embedding rows equal the fixture's bytes, and the
+    oracle forward over them reproduces the reference's own logits and layer-0 output."""
+    from oracle import hybrid as HY
+    from oracle import synth_qwen35 as SQ
+    z = np.load(os.path.join(GOLDEN, "synth_qwen35_fixture.npz"))
+    cfg, W = SQ.synth_weights()
+    ids = SQ.synth_ids()
+    assert np.array_equal(ids, z["ids"])
+    assert np.array_equal(W["embed"][ids][-32:], z["embed_tail"])
+    out = HY.forward(W, cfg, ids)
+    assert np.abs(out["layers"][0] - z["layer0"]).max() < 1e-3
+    assert np.abs(out["logits"] - z["logits"]).max() < 1e-3
+    assert int(out["logits"][-1].argmax()) == int(z["argmax_last"]) == 201

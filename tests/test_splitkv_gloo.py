@@ -86,3 +86,55 @@ def test_splitkv_two_ranks_matches_single(L):
     assert (lo0, hi1) == (0, L) and hi0 == lo1
     for o in (o0, o1):                       # every rank ends with the full result
         assert np.abs(o[0] - exp).max() < 1e-5
+
+
+def _failing_worker(rank, world, port, how, ret):
+    """Rank 1 fails between steps (``raise``: an exception ends the process; ``stall``: it stays
+    alive but never joins step 2); rank 0 must come back from step 2 with PeerFailure."""
+    import datetime
+    import sys
+    import time
+    sys.path.insert(0, ROOT)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    from bitgpu_b200.splitkv import PeerFailure, SplitKVDecoder
+    rng = np.random.default_rng(0)
+    L, B, S, H, KV, D = 96, 1, 1, 2, 1, 64
+    K = rng.standard_normal((B, L, KV, D)).astype(np.float32)
+    V = rng.standard_normal((B, L, KV, D)).astype(np.float32)
+    q = torch.from_numpy(rng.standard_normal((B, S, H, D)).astype(np.float32))
+    dec = SplitKVDecoder(L, partials_fn=lambda q_, c, pb, lo, hi, sc: _oracle_partials(q_, c, pb, lo, hi, sc),
+                         merge_fn=_oracle_merge)
+    dec.step(q, (K, V), L - 1)                     # step 1 completes on both ranks
+    if rank == 1:
+        if how == "raise":
+            raise SystemExit(3)                    # the process ends between steps
+        time.sleep(30)                             # alive, but never joins step 2
+        return
+    t0 = time.time()
+    try:
+        dec.step(q, (K, V), L - 1)
+        ret[0] = ("no error", time.time() - t0)
+    except PeerFailure as e:
+        ret[0] = ("PeerFailure", time.time() - t0, str(e)[:200])
+    os._exit(0)                                    # the group is broken; skip its teardown
+
+
+@pytest.mark.parametrize("how", ["raise", "stall"])
+def test_splitkv_peer_failure_is_reported(how):
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    ret = manager.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, 2, port, how, ret)) for r in range(2)]
+    for p in procs:
+        p.start()
+    procs[0].join(90)
+    alive = procs[0].is_alive()
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+        p.join(10)
+    assert not alive, "the surviving rank hung"
+    assert ret[0][0] == "PeerFailure", ret.get(0)
+    assert ret[0][1] < 60

@@ -47,22 +47,23 @@ def test_noalloc_matches_workspace_entry_point_twice():
     from bitgpu_b200 import ops
     from bitgpu_b200._lib import lib
     L = lib()
-    # first call on this device also performs the one-time scratch address lookup
     _call_pair(L, ops, "f16", B=4, S=1, H=32, KV=8, D=128, pos_base=4095, seed=1, gated=False)
     # second call: different shape, cache codec and gate; reuses the same scratch array
     _call_pair(L, ops, "q8", B=1, S=3, H=24, KV=4, D=256, pos_base=2000, seed=2, gated=True)
 
 
 def test_noalloc_rejects_oversized_scratch(monkeypatch):
-    """A call whose split partials would exceed the fixed 8 MiB is refused (BG_ENOMEM) before any
-    launch.  The split-count override forces 64 splits of 2048 rows (68 MB of partials)."""
+    """A call whose split partials would exceed the fixed scratch (bg_attention_noalloc_limit(),
+    8 MiB) is refused (BG_ENOMEM) before any launch.  The split-count override forces 64 splits of
+    2048 rows (68 MB of partials)."""
     from bitgpu_b200 import ops
     from bitgpu_b200._lib import AttnParams, BG_ENOMEM, DT_F32, lib
     L = lib()
     monkeypatch.setenv("BGATTN_NSPLIT", "64")
     B, S, H, KV, D = 64, 1, 32, 8, 128
     p = AttnParams(S, H, KV, D, 32767, 32768)
-    assert L.bg_attention_workspace_size(C.byref(p), B) > 8 << 20
+    assert L.bg_attention_noalloc_limit() == 8 << 20
+    assert L.bg_attention_workspace_size(C.byref(p), B) > L.bg_attention_noalloc_limit()
     cache = ops.KVCache(1, 8, KV, D, mode="f16")
     d = cache.desc()
     rc = L.bg_attention_noalloc(C.byref(p), B, C.c_void_p(1), DT_F32, C.byref(d), None, None, 0.0, None,
