@@ -279,18 +279,23 @@ def prefill_flops(batch, seq):
     return 4.0 * D * PF_H * batch * seq * (seq + 1) / 2
 
 
-def run_prefill(torch, ops, args, rank, barrier, max_over_ranks, clocks_for=None):
-    """Config 3: causal prefill attention of `batch` x `seq` f16 tokens over the f16 cache those
-    tokens were appended to (posBase 0), f16 output; then the step's K/V rows written into an f16
-    and a q8 cache (timed separately, as bytes)."""
+def run_prefill(torch, ops, args, rank, barrier, max_over_ranks, clocks_for=None, mode="f16", q32=False,
+                kv_write=True):
+    """Config 3: causal prefill attention of `batch` x `seq` tokens over the cache those tokens
+    were appended to (posBase 0), f16 output.  Default: f16 queries over an f16 cache (BASELINE's
+    wording); mode="q8", q32=True is the engine's own call (f32 queries over the 8-bit cache,
+    engine.ts:1580).  Then the step's K/V rows written into an f16 and a q8 cache (timed
+    separately, as bytes)."""
     nb, S = args.prefill_batch, args.seq
     g = torch.Generator(device="cuda").manual_seed(7 + rank)
     k16 = torch.randn((nb, S, PF_KV, D), generator=g, device="cuda").half()
     v16 = torch.randn((nb, S, PF_KV, D), generator=g, device="cuda").half()
-    cache = ops.KVCache(nb, S, PF_KV, D, mode="f16", device="cuda")
+    cache = ops.KVCache(nb, S, PF_KV, D, mode=mode, device="cuda")
     cache.append(0, k16, 0)
     cache.append(1, v16, 0)
-    q = torch.randn((nb, S, PF_H, D), generator=g, device="cuda").half()
+    q = torch.randn((nb, S, PF_H, D), generator=g, device="cuda")
+    if not q32:
+        q = q.half()
     out = torch.empty((nb, S, PF_H, D), device="cuda", dtype=torch.float16)
     clk = Clocks(clocks_for) if clocks_for is not None else None
     ms = max_over_ranks(time_steps(torch, lambda: ops.attention(q, cache, 0, out=out), args.steps, args.warmup,
@@ -298,6 +303,10 @@ def run_prefill(torch, ops, args, rank, barrier, max_over_ranks, clocks_for=None
     res = {"ms": ms, "flops": prefill_flops(nb, S)}
     if clk:
         res["clocks"] = clk.stop()
+    if not kv_write:
+        del cache, q, out
+        torch.cuda.empty_cache()
+        return res
     # the prefill's K/V written into an f16 cache and a q8 cache (kv append, HBM-bound)
     c16 = ops.KVCache(nb, S, PF_KV, D, mode="f16", device="cuda")
     c8 = ops.KVCache(nb, S, PF_KV, D, mode="q8", device="cuda")
@@ -611,6 +620,12 @@ def run_ours(args):
                             "unit": "TFLOP/s", "ms_per_step": round(pf["ms"], 4), "frac": round(tf / bf16_peak, 4),
                             "peak": bf16_peak, "peak_kind": f"{peak_kind} cuBLAS bf16 burst",
                             "flops_per_step_per_gpu": pf["flops"], "kv_write": pf["kv_write"]}
+        pq = run_prefill(torch, ops, short, rank, barrier, max_over_ranks, mode="q8", q32=True, kv_write=False)
+        tq = pq["flops"] / (pq["ms"] * 1e-3) / 1e12
+        extra["prefill_q8_f32q"] = {"metric": "prefill-attn TFLOP/s (config 3 shape, f32 queries over a q8 cache: "
+                                              "the engine's own prefill call)", "value": round(tq * ws, 2),
+                                    "unit": "TFLOP/s", "ms_per_step": round(pq["ms"], 4),
+                                    "frac": round(tq / bf16_peak, 4), "peak": bf16_peak}
     if "gated" in variants:
         gs = argparse.Namespace(**vars(short))
         gs.steps = max(20, short.steps)

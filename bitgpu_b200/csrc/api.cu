@@ -66,14 +66,21 @@ int run_attention(const bg_attn_params *p, uint32_t batch, const void *q, uint32
                   uint32_t row_offset, float *partials_out, const float *gate, void *out, uint32_t out_dtype,
                   void *ws, size_t ws_bytes, cudaStream_t st) {
   const float sc = scale > 0.f ? scale : 1.0f / sqrtf((float)p->D);
-  // dense prefill on the tensor cores (f16 queries over an f16 cache, whole causal range)
-  if (!partials_out && !gate && !g_force_generic &&
-      prefill_tc_supported((int)kv->mode, p->D, p->S, q_dtype == BG_DT_F16, cosT != nullptr, kv->window != 0)) {
+  // dense prefill on the tensor cores (f16 / f32 queries over an f16 or q8 cache, whole causal
+  // range, optional sigmoid gate)
+  if (!partials_out && !g_force_generic &&
+      prefill_tc_supported((int)kv->mode, p->D, p->S, cosT != nullptr, kv->window != 0)) {
     PrefillArgs pa;
     pa.q = q;
+    pa.q_f32 = q_dtype == BG_DT_F32;
+    pa.mode = (int)kv->mode;
+    pa.D = p->D;
     pa.K = kv->K;
     pa.V = kv->V;
+    pa.Ks = kv->Ks;
+    pa.Vs = kv->Vs;
     pa.seq_stride = kv->seq_stride;
+    pa.gate = gate;
     pa.out = out;
     pa.out_f16 = out_dtype == BG_DT_F16;
     pa.B = batch;
@@ -83,6 +90,8 @@ int run_attention(const bg_attn_params *p, uint32_t batch, const void *q, uint32
     pa.posBase = p->posBase;
     pa.Ltot = p->Ltot;
     pa.scale = sc;
+    pa.ws = ws;
+    pa.ws_bytes = ws_bytes;
     return launch_prefill_tc(pa, st);
   }
   AttnArgs a;
@@ -187,6 +196,16 @@ int snapshot_copy(const bg_kv_cache *kv, uint32_t seq, uint32_t KV, uint32_t D, 
 
 }  // namespace
 
+namespace bg {
+size_t attention_split_workspace_bytes(const bg_attn_params *p, uint32_t batch) {
+  if (!p || !p->KV || !p->H) return 0;
+  const uint32_t L = p->Ltot ? p->Ltot : 1;
+  uint32_t ns = attn_max_splits(batch, p->S, p->H, p->KV, p->D, L);
+  if (env_nsplit() > ns) ns = env_nsplit();
+  return ns > 1 ? part_bytes(ns, (uint64_t)batch * p->S * p->H, p->D) : 0;  // one split needs no scratch
+}
+}  // namespace bg
+
 extern "C" {
 
 size_t bg_kv_snapshot_bytes(const bg_kv_cache *kv, uint32_t KV, uint32_t D, uint32_t count) {
@@ -221,6 +240,7 @@ const char *bg_strerror(int code) {
 
 int bg_version(void) { return 1; }
 
+
 int bg_force_generic(int on) {
   const int prev = g_force_generic;
   g_force_generic = on ? 1 : 0;
@@ -238,10 +258,13 @@ int bg_device_status(bg_stream_t stream) {
 
 size_t bg_attention_workspace_size(const bg_attn_params *p, uint32_t batch) {
   if (!p || !p->KV || !p->H) return 0;
-  const uint32_t L = p->Ltot ? p->Ltot : 1;
-  uint32_t ns = attn_max_splits(batch, p->S, p->H, p->KV, p->D, L);
-  if (env_nsplit() > ns) ns = env_nsplit();
-  return ns > 1 ? part_bytes(ns, (uint64_t)batch * p->S * p->H, p->D) : 0;  // one split needs no scratch
+  size_t split = attention_split_workspace_bytes(p, batch);
+  // a tensor-core prefill over a q8 cache dequantises it once into this workspace when it fits
+  if (prefill_tc_supported(BG_KV_Q8, p->D, p->S, false, false)) {
+    const size_t cp = prefill_q8_copy_bytes(batch, p->Ltot, p->KV, p->D);
+    if (cp > split) split = cp;
+  }
+  return split;
 }
 
 int bg_attention(const bg_attn_params *p, uint32_t batch, const void *q, uint32_t q_dtype, const bg_kv_cache *kv,

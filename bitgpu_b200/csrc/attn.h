@@ -46,6 +46,8 @@ bool roll_legacy();  // BGATTN_ROLL_LEGACY=1 selects the one-head-per-CTA kernel
 
 // Read-and-clear the bounded-wait timeout flag of the TMA kernels (BG_ETIMEOUT or 0).
 int poll_device_error_attn_tc();
+// Split-KV partial scratch a bg_attention call may need (the part every kernel path shares).
+size_t attention_split_workspace_bytes(const bg_attn_params *p, uint32_t batch);
 int poll_device_error_attn_roll();
 
 }  // namespace bg

@@ -37,8 +37,9 @@ int bg_attention_noalloc(const bg_attn_params *p, uint32_t batch, const void *q,
                          const bg_kv_cache *kv, const float *cosT, const float *sinT, float scale, const float *gate,
                          void *out, uint32_t out_dtype, bg_stream_t stream) {
   if (!p) return BG_EINVAL;
-  // Shapes whose partials do not fit the fixed scratch are rejected up front (BG_ENOMEM).
-  if (bg_attention_workspace_size(p, batch) > kNoAllocScratchBytes) return BG_ENOMEM;
+  // Shapes whose split partials do not fit the fixed scratch are rejected up front (BG_ENOMEM).  A
+  // q8 prefill too large to dequantise into the scratch dequantises inside its kernel instead.
+  if (bg::attention_split_workspace_bytes(p, batch) > kNoAllocScratchBytes) return BG_ENOMEM;
   void *ws = scratch_for_current_device();
   if (!ws) return BG_ELAUNCH;
   // Every partial row the merge reads is written earlier in the same call, so the scratch needs

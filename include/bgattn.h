@@ -87,7 +87,10 @@ int bg_force_generic(int on);
  * scale == 0 selects 1/sqrt(D) (attention_sg.wgsl:24); the online kernels pass it explicitly.
  * cosT/sinT non-NULL selects rope-at-read of unroped keys by logical slot, tables
  * [positions][D/2] (the attention_*_roll.wgsl kernels, bindings engine.ts:1395-1399).
- * gate [batch][S][H][D] f32 or NULL: out = att / (1 + exp(-gate)). */
+ * gate [batch][S][H][D] f32 or NULL: out = att / (1 + exp(-gate)).
+ * Workspace: bg_attention_workspace_size bytes covers split-KV partials and, for a prefill
+ * (S >= 64) over a q8 cache, an f16 copy of the cache positions [0, Ltot) that the tensor-core
+ * prefill dequantises into once; with less, that prefill dequantises inside its kernel. */
 size_t bg_attention_workspace_size(const bg_attn_params *p, uint32_t batch);
 int bg_attention(const bg_attn_params *p, uint32_t batch, const void *q, uint32_t q_dtype,
                  const bg_kv_cache *kv, const float *cosT, const float *sinT, float scale,
@@ -101,8 +104,9 @@ int bg_attention(const bg_attn_params *p, uint32_t batch, const void *q, uint32_
  * (which can synchronise the device).  This variant takes no workspace: it uses a fixed
  * BG_NOALLOC_SCRATCH_BYTES (8 MiB) scratch array compiled into the library, held on every GPU
  * that loads the library until the process exits.  Same arguments and results as bg_attention
- * minus the workspace; returns BG_ENOMEM when bg_attention_workspace_size(p, batch) exceeds the
- * limit (bg_attention_noalloc_limit() reports it).  Every call looks up the array's device
+ * minus the workspace; returns BG_ENOMEM when the call's split-KV partials exceed the limit
+ * (bg_attention_noalloc_limit() reports it); a q8 prefill too large to dequantise into the array
+ * dequantises inside its kernel instead.  Every call looks up the array's device
  * address in the current context (so it stays right after cudaDeviceReset); make the first call
  * on a device before any stream capture.  All calls share the one array: calls that overlap on
  * the GPU (different streams, or several host threads) race on it and must be serialised by the

@@ -23,28 +23,42 @@ def half_ulp(x):
     return (np.spacing(x).astype(np.float32)) * 0.5
 
 
-@pytest.mark.parametrize("B,S,H,KV,pos_base,out16", [
-    (2, 300, 32, 8, 0, True),      # ragged S (not a multiple of 256), GQA 4
-    (1, 256, 16, 8, 0, False),     # exactly one block, GQA 2, f32 output
-    (1, 200, 32, 8, 77, True),     # continuing segment: posBase > 0 (engine prefill segments)
-    (1, 64, 8, 8, 1000, True),     # smallest S on this path, MHA, long prefix
+@pytest.mark.parametrize("mode", ["f16", "q8"])
+@pytest.mark.parametrize("q32", [False, True])
+@pytest.mark.parametrize("B,S,H,KV,D,pos_base,out16,gated", [
+    (2, 300, 32, 8, 128, 0, True, False),     # ragged S (not a multiple of 256), GQA 4
+    (1, 256, 16, 8, 128, 0, False, False),    # exactly one block, GQA 2, f32 output
+    (1, 200, 32, 8, 128, 77, True, False),    # continuing segment: posBase > 0 (engine prefill segments)
+    (1, 64, 8, 8, 128, 1000, True, False),    # smallest S on this path, MHA, long prefix
+    (1, 256, 24, 4, 256, 0, False, True),     # the 27B hybrid's gated head_dim-256 prefill segment
+    (1, 200, 24, 4, 256, 3000, False, True),  # ... continuing after a long context
+    (2, 130, 8, 2, 256, 5, True, False),      # head_dim 256, ragged, f16 output, no gate
 ])
-def test_prefill_vs_oracle(ops, B, S, H, KV, pos_base, out16):
-    rng = np.random.default_rng(S + H + pos_base)
-    D = 128
+def test_prefill_vs_oracle(ops, mode, q32, B, S, H, KV, D, pos_base, out16, gated):
+    """tcgen05 prefill over f16 and q8 caches with f16 and f32 queries (the engine's call passes
+    f32 queries, engine.ts:1580), head_dim 128 and the gated head_dim 256, vs the oracle."""
+    rng = np.random.default_rng(S + H + pos_base + D)
     L = pos_base + S
-    cache = ops.KVCache(B, L + 7, KV, D, mode="f16")
+    cache = ops.KVCache(B, L + 7, KV, D, mode=mode)
     Kd, Vd = fill_cache(cache, rand(rng, B, L, KV, D), rand(rng, B, L, KV, D))
-    q = rand(rng, B, S, H, D).astype(np.float16)
-    out = ops.attention(torch.from_numpy(q).cuda(), cache, pos_base,
+    q = rand(rng, B, S, H, D)
+    if not q32:
+        q = q.astype(np.float16)
+    gate = rand(rng, B, S, H, D) if gated else None
+    scale = 1.0 / np.sqrt(D)
+    out = ops.attention(torch.from_numpy(q).cuda(), cache, pos_base, scale=scale,
+                        gate=torch.from_numpy(gate).cuda() if gated else None,
                         out_dtype=torch.float16 if out16 else torch.float32).float().cpu().numpy()
     for b in range(B):
-        exp = OA.attend(q[b].astype(np.float32), Kd[b], Vd[b], pos_base)
+        exp = OA.attend(q[b].astype(np.float32), Kd[b], Vd[b], pos_base, scale=scale,
+                        gate=gate[b] if gated else None)
         bound = 2e-3 + (half_ulp(exp) if out16 else 0.0)
         err = np.abs(out[b] - exp)
         assert np.all(err <= bound), (b, float(err.max()), float((err - bound).max()))
         cos = float((out[b] * exp).sum() / (np.linalg.norm(out[b]) * np.linalg.norm(exp)))
         assert cos > 0.99999
+    from bitgpu_b200._lib import lib
+    assert lib().bg_device_status(None) == 0
 
 
 def test_prefill_vs_generic_long(ops):
@@ -63,4 +77,30 @@ def test_prefill_vs_generic_long(ops):
     finally:
         lib().bg_force_generic(prev)
     assert (a - b).abs().max().item() < 2e-3
+    assert lib().bg_device_status(None) == 0
+
+
+@pytest.mark.parametrize("D,H,KV", [(128, 32, 8), (256, 24, 4)])
+def test_prefill_q8_fused_equals_prepass(ops, D, H, KV):
+    """A q8 prefill dequantises the cache once into the workspace when it has room (the path
+    ops.attention takes), else inside every CTA (no workspace): both vs the oracle."""
+    import ctypes as C
+    from bitgpu_b200._lib import AttnParams, DT_F32, lib
+    rng = np.random.default_rng(D)
+    B, S = 1, 512
+    cache = ops.KVCache(B, S, KV, D, mode="q8")
+    Kd, Vd = fill_cache(cache, rand(rng, B, S, KV, D), rand(rng, B, S, KV, D))
+    q = torch.from_numpy(rand(rng, B, S, H, D)).cuda()
+    a = ops.attention(q, cache, 0)
+    p = AttnParams(S, H, KV, D, 0, S)
+    d = cache.desc()
+    b = torch.empty_like(q)
+    rc = lib().bg_attention(C.byref(p), B, C.c_void_p(q.data_ptr()), DT_F32, C.byref(d), None, None, 0.0, None,
+                            C.c_void_p(b.data_ptr()), DT_F32, None, 0,
+                            C.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0
+    exp = OA.attend(q[0].cpu().numpy(), Kd[0], Vd[0], 0)
+    for out in (a, b):
+        err = np.abs(out[0].cpu().numpy() - exp).max()
+        assert err < 2e-3, err
     assert lib().bg_device_status(None) == 0
