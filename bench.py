@@ -279,6 +279,33 @@ def prefill_flops(batch, seq):
     return 4.0 * D * PF_H * batch * seq * (seq + 1) / 2
 
 
+def tf32_peak(torch, n=8192, reps=10):
+    """Dense TF32 tensor-core throughput measured here: torch.matmul of two n x n f32 matrices
+    with TF32 allowed (cuBLAS), best of `reps`, 2*n^3 flops per product."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    try:
+        a = torch.randn((n, n), device="cuda")
+        b = torch.randn((n, n), device="cuda")
+        c = a @ b
+        best = None
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch.matmul(a, b, out=c)
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1)
+            best = ms if best is None else min(best, ms)
+        del a, b, c
+        torch.cuda.empty_cache()
+        return {"tflops": round(2.0 * n ** 3 / (best * 1e-3) / 1e12, 1), "how": f"cuBLAS TF32 matmul {n}^3, best of {reps}"}
+    except Exception as e:  # noqa: BLE001
+        return {"tflops": None, "how": f"unavailable: {e}"}
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
 def run_prefill(torch, ops, args, rank, barrier, max_over_ranks, clocks_for=None, mode="f16", q32=False,
                 kv_write=True):
     """Config 3: causal prefill attention of `batch` x `seq` tokens over the cache those tokens
@@ -620,6 +647,14 @@ def run_ours(args):
                             "unit": "TFLOP/s", "ms_per_step": round(pf["ms"], 4), "frac": round(tf / bf16_peak, 4),
                             "peak": bf16_peak, "peak_kind": f"{peak_kind} cuBLAS bf16 burst",
                             "flops_per_step_per_gpu": pf["flops"], "kv_write": pf["kv_write"]}
+        pf32 = run_prefill(torch, ops, short, rank, barrier, max_over_ranks, mode="f32", q32=True, kv_write=False)
+        t32 = pf32["flops"] / (pf32["ms"] * 1e-3) / 1e12
+        tf32_pk = tf32_peak(torch)
+        extra["prefill_f32kv_3xtf32"] = {
+            "metric": "prefill-attn TFLOP/s (config 3 shape, f32 queries over an f32 cache, 3xTF32 on tcgen05)",
+            "value": round(t32 * ws, 2), "unit": "TFLOP/s", "ms_per_step": round(pf32["ms"], 4),
+            "flops_note": "algorithmic flops (QK^T + PV once); the kernel issues 3 S and 3 PV tf32 products (x3 executed)",
+            "tf32_peak": tf32_pk, "frac_of_tf32_peak": round(t32 / tf32_pk["tflops"], 4) if tf32_pk["tflops"] else None}
         pq = run_prefill(torch, ops, short, rank, barrier, max_over_ranks, mode="q8", q32=True, kv_write=False)
         tq = pq["flops"] / (pq["ms"] * 1e-3) / 1e12
         extra["prefill_q8_f32q"] = {"metric": "prefill-attn TFLOP/s (config 3 shape, f32 queries over a q8 cache: "

@@ -66,8 +66,8 @@ int run_attention(const bg_attn_params *p, uint32_t batch, const void *q, uint32
                   uint32_t row_offset, float *partials_out, const float *gate, void *out, uint32_t out_dtype,
                   void *ws, size_t ws_bytes, cudaStream_t st) {
   const float sc = scale > 0.f ? scale : 1.0f / sqrtf((float)p->D);
-  // dense prefill on the tensor cores (f16 / f32 queries over an f16 or q8 cache, whole causal
-  // range, optional sigmoid gate)
+  // dense prefill on the tensor cores (f16 / f32 queries over an f16 or q8 cache, or an f32 cache
+  // in 3xTF32; whole causal range, optional sigmoid gate)
   if (!partials_out && !g_force_generic &&
       prefill_tc_supported((int)kv->mode, p->D, p->S, cosT != nullptr, kv->window != 0)) {
     PrefillArgs pa;
@@ -253,6 +253,7 @@ int bg_device_status(bg_stream_t stream) {
   if (!e) e = poll_device_error_attn_roll();
   if (!e) e = poll_device_error_prefill();
   if (!e) e = poll_device_error_selftest();
+  if (!e) e = poll_device_error_prefill_tf32();
   return e ? (e < 0 ? e : BG_ELAUNCH) : BG_OK;
 }
 

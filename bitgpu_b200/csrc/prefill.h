@@ -7,7 +7,7 @@ namespace bg {
 struct PrefillArgs {
   const void *q;          // [B][S][H][D] f32 (q_f32) or f16
   int q_f32;
-  int mode;               // BG_KV_F16 or BG_KV_Q8
+  int mode;               // BG_KV_F16, BG_KV_Q8 or BG_KV_F32 (head_dim 128)
   uint32_t D;             // 128 or 256
   const void *K, *V;      // cache [B][seq_stride][KV][D]: f16 values or int8 codes
   const float *Ks, *Vs;   // q8 block scales [B][seq_stride][KV][D/32]
@@ -28,6 +28,8 @@ inline size_t prefill_q8_copy_bytes(uint32_t B, uint32_t Ltot, uint32_t KV, uint
 
 bool prefill_tc_supported(int mode, uint32_t D, uint32_t S, bool roll, bool ring);
 int launch_prefill_tc(const PrefillArgs &a, cudaStream_t st);
+int launch_prefill_tf32(const PrefillArgs &a, cudaStream_t st);  // f32 cache, 3xTF32
+int poll_device_error_prefill_tf32();
 int poll_device_error_prefill();
 int poll_device_error_selftest();
 

@@ -35,6 +35,7 @@
 
 #include "prefill.h"
 #include "tma.cuh"
+#include "umma.cuh"
 
 namespace bg {
 namespace {
@@ -74,94 +75,6 @@ struct PfParams {
   float sl2;
 };
 
-__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
-         ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46) /*sm100 descriptor*/ | (2ull << 61) /*SW128*/;
-}
-
-// kind::f16 instruction descriptor: f32 accumulate, f16 A/B, M=128, N=n.
-constexpr uint32_t idesc_f16(int n, bool b_mn_major) {
-  return (1u << 4) | (b_mn_major ? (1u << 16) : 0u) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-}
-
-__device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc));
-}
-
-__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t *bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-#define BG_R32(r) r[0], r[1], r[2], r[3], r[4], r[5], r[6], r[7], r[8], r[9], r[10], r[11], r[12], r[13], r[14], r[15], \
-                  r[16], r[17], r[18], r[19], r[20], r[21], r[22], r[23], r[24], r[25], r[26], r[27], r[28], r[29],  \
-                  r[30], r[31]
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
-      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-}
-
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
-      "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
-      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
-      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
-      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
-          taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
-      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
-      : "memory");
-}
-
-__device__ __forceinline__ float ex2_approx(float x) {  // MUFU exp2; exp2(-inf) = +0
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-__device__ __forceinline__ float fmax3(float a, float b, float c) {  // 3-input max (sm_100)
-  float d;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
-
-__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
-  __half2 h = __floats2half2_rn(lo, hi);
-  return *reinterpret_cast<uint32_t *>(&h);
-}
-
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-
-
 // Byte offset of 16-byte chunk `ch` (8 f16 of one row) of row r in a 128B-swizzled K-major f16
 // operand tile of R rows: column blocks of 64 elements, each R rows x 128 B.
 template <int R>
@@ -169,8 +82,6 @@ __device__ __forceinline__ uint32_t sw128_off(int r, int ch) {
   return (uint32_t)((ch >> 3) * (R * 128) + r * 128 + (((ch & 7) ^ (r & 7)) << 4));
 }
 
-// Generic-proxy writes to shared memory become visible to the tensor cores' async proxy.
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // 16 int8 codes with one block scale (s / 127 as f16x2) -> 16 f16 values code * s / 127.  The
 // codes become exact f16 integers through the exponent trick: byte (c + 128) under the f16
@@ -501,11 +412,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       // lazy rescale; the TMEM round trip is .sync.aligned, so the branch is taken by the whole
       // warp when any of its rows moved, and rows that did not move use the factor 1
       const bool need = mt > m_used + kRescaleThreshold;
+      // head_dim 128: PV_t(j-1) has completed (the commit we waited on, after S_t(j), covers it).
+      // head_dim 256: S(j) was issued before PV(j-1), so PV(j-1) may still run; its o_done phase
+      // is consumed exactly once, in order (here, or at the end of this step), so that no wait on
+      // o_done can ever be two phases behind the barrier.
+      bool pv_prev_done = NQT == 2 || j == 0;
       if (__any_sync(0xffffffffu, need)) {
         if (j > 0) {
-          // head_dim 128: PV_t(j-1) has completed (the commit we waited on, after S_t(j), covers
-          // it).  head_dim 256: S(j) was issued before PV(j-1), so wait for PV(j-1) itself.
-          if (NQT == 1 && !mbar_wait_warp(&o_done[0], (j - 1) & 1)) { ok = false; break; }
+          if (!pv_prev_done && !mbar_wait_warp(&o_done[0], (j - 1) & 1)) { ok = false; break; }
+          pv_prev_done = true;
           tc_fence_after();
           const float f = (need && m_used > -INFINITY) ? ex2_approx(m_used - mt) : 1.0f;
           const uint32_t obase = (tmem + otile) | lane_off;
@@ -545,6 +460,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       l += ls0 + ls1;
       tmem_wait_st();
+      if (!pv_prev_done && !mbar_wait_warp(&o_done[0], (j - 1) & 1)) { ok = false; break; }
       tc_fence_before();
       mbar_arrive(&p_full[slot_i]);
     }
@@ -683,10 +599,12 @@ __global__ void __launch_bounds__(256) dequant_q8_kernel(const int8_t *__restric
 }  // namespace
 
 bool prefill_tc_supported(int mode, uint32_t D, uint32_t S, bool roll, bool ring) {
-  return (mode == BG_KV_F16 || mode == BG_KV_Q8) && (D == 128 || D == 256) && !roll && !ring && S >= 64;
+  const bool shape = (mode == BG_KV_F16 || mode == BG_KV_Q8) ? (D == 128 || D == 256) : (mode == BG_KV_F32 && D == 128);
+  return shape && !roll && !ring && S >= 64;
 }
 
 int launch_prefill_tc(const PrefillArgs &a, cudaStream_t st) {
+  if (a.mode == BG_KV_F32) return launch_prefill_tf32(a, st);
   const bool q8 = a.mode == BG_KV_Q8;
   // q8 with room in the workspace and a prefill that reads every position many times (S large
   // against Ltot): dequantise the cache once into f16 copies, then run the TMA f16 kernel.  The

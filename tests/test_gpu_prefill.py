@@ -23,7 +23,7 @@ def half_ulp(x):
     return (np.spacing(x).astype(np.float32)) * 0.5
 
 
-@pytest.mark.parametrize("mode", ["f16", "q8"])
+@pytest.mark.parametrize("mode", ["f16", "q8", "f32"])
 @pytest.mark.parametrize("q32", [False, True])
 @pytest.mark.parametrize("B,S,H,KV,D,pos_base,out16,gated", [
     (2, 300, 32, 8, 128, 0, True, False),     # ragged S (not a multiple of 256), GQA 4
@@ -36,7 +36,8 @@ def half_ulp(x):
 ])
 def test_prefill_vs_oracle(ops, mode, q32, B, S, H, KV, D, pos_base, out16, gated):
     """tcgen05 prefill over f16 and q8 caches with f16 and f32 queries (the engine's call passes
-    f32 queries, engine.ts:1580), head_dim 128 and the gated head_dim 256, vs the oracle."""
+    f32 queries, engine.ts:1580), head_dim 128 and the gated head_dim 256, and over an f32 cache
+    in 3xTF32 (head_dim 128; head_dim 256 f32 runs on the CUDA-core kernel), vs the oracle."""
     rng = np.random.default_rng(S + H + pos_base + D)
     L = pos_base + S
     cache = ops.KVCache(B, L + 7, KV, D, mode=mode)
@@ -104,3 +105,18 @@ def test_prefill_q8_fused_equals_prepass(ops, D, H, KV):
         err = np.abs(out[0].cpu().numpy() - exp).max()
         assert err < 2e-3, err
     assert lib().bg_device_status(None) == 0
+
+
+def test_prefill_f32_3xtf32_precision(ops):
+    """The 3xTF32 split (hi/lo operands, three products each for Q K^T and P V) keeps the f32
+    cache's prefill at f32-class accuracy: errors near 1e-6 against the oracle, where one TF32
+    product per matrix would sit near 1e-3."""
+    rng = np.random.default_rng(123)
+    B, S, H, KV, D = 1, 512, 16, 4, 128
+    cache = ops.KVCache(B, S, KV, D, mode="f32")
+    Kd, Vd = fill_cache(cache, rand(rng, B, S, KV, D), rand(rng, B, S, KV, D))
+    q = rand(rng, B, S, H, D)
+    out = ops.attention(torch.from_numpy(q).cuda(), cache, 0).cpu().numpy()
+    exp = OA.attend(q[0], Kd[0], Vd[0], 0)
+    err = float(np.abs(out[0] - exp).max())
+    assert err < 5e-5, err
