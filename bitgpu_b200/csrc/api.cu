@@ -254,6 +254,7 @@ int bg_device_status(bg_stream_t stream) {
   if (!e) e = poll_device_error_prefill();
   if (!e) e = poll_device_error_selftest();
   if (!e) e = poll_device_error_prefill_tf32();
+  if (!e) e = poll_device_error_deltanet();
   return e ? (e < 0 ? e : BG_ELAUNCH) : BG_OK;
 }
 

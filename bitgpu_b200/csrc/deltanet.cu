@@ -15,6 +15,7 @@
 #include <stdlib.h>
 
 #include "kv.h"
+#include "tma.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -387,6 +388,201 @@ __global__ void __launch_bounds__(512) deltanet_head_vec_kernel(DeltaArgs a) {
   }
 }
 
+// Decode (calls of at most 16 tokens) for DK = DV = 128: the state columns of a head split over a
+// cluster of kSplitCTAs CTAs (kSplitCols columns each), so a 48-head layer runs 384 CTAs across all
+// SMs instead of 48 and each SM moves ~1/148 of the state.  Thread (row group rg, column group cg)
+// holds rows [4 rg, 4 rg + 4) x columns [4 cg, 4 cg + 4) of the CTA's slice: the state moves as
+// four float4 loads and stores per thread.  The two reductions over dk per token run as warp
+// shuffles plus one shared-memory pass over the CTA's warps; the gated norm's sum of squares over
+// all 128 columns crosses the cluster one way: every CTA stores its partial into each peer's
+// shared memory with st.async, which counts the bytes on the peer's mbarrier, and waits on its own
+// mbarrier for all partials (double-buffered by token parity) -- no cluster-wide barrier per token.
+template <bool FUSED, int NC>
+__global__ void __launch_bounds__(NC * 8) deltanet_split_kernel(DeltaArgs a) {
+  constexpr int DK = 128, DV = 128, CG = NC / 4, NT = NC * 8, NW = NT / 32, kSplitCTAs = 128 / NC;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int cg_ = tid % CG, rg = tid / CG;           // 32 row groups of 4 rows
+  const uint32_t split = blockIdx.x, h = blockIdx.y, hk = h % a.HK;
+  const int r0 = 4 * rg, col = (int)split * NC + 4 * cg_;
+  // Programmatic dependent launch: let the next kernel of the stream get scheduled now; it waits
+  // in its own griddepcontrol.wait until this grid has completed and its writes are visible.
+  // Nothing is read before this grid's own wait (the previous kernel may produce any input,
+  // the state included).
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // While the previous kernel may still run, warm L2 with this thread's state rows: a prefetch
+  // returns no data, and L2 stays coherent with whatever that kernel writes, so this is safe.
+  if (a.loadState && a.state_in && a.S) {
+    const float *sp = a.state_in + (uint64_t)h * 128 * 128 + (uint64_t)r0 * 128 + col;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) asm volatile("prefetch.global.L2 [%0];" ::"l"(sp + i * 128));
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  __shared__ __align__(16) float kn_s[DK], qn_s[DK];
+  __shared__ __align__(16) float red_kv[NW][NC], red_o[NW][NC];
+  __shared__ float ss_in[2][8];                 // partial sums of squares from each cluster rank
+  __shared__ __align__(8) uint64_t ss_bar[2];   // their arrival, by token parity
+  uint32_t my_rank = 0;
+  if constexpr (FUSED) {
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(my_rank));
+    if (tid == 0) {
+      mbar_init(&ss_bar[0], 1);
+      mbar_init(&ss_bar[1], 1);
+      fence_barrier_init();
+    }
+    // peers may store into this CTA only after its barriers exist: arrive now, wait before the
+    // first exchange (the state loads in between hide the barrier latency)
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  }
+
+  float kq[4] = {0.f, 0.f, 0.f, 0.f}, ga = 0.f, gb = 0.f;
+  float4 vv = make_float4(0.f, 0.f, 0.f, 0.f), zz = vv;
+  auto load_inputs = [&](uint32_t t) {
+    const uint32_t tt = t + a.tOff;
+    const uint64_t base = (uint64_t)tt * a.H + h, basek = (uint64_t)tt * a.HK + hk;
+    if (warp < 2) {
+      const float4 x = *reinterpret_cast<const float4 *>((warp ? a.q : a.k) + basek * DK + lane * 4);
+      kq[0] = x.x; kq[1] = x.y; kq[2] = x.z; kq[3] = x.w;
+    }
+    vv = *reinterpret_cast<const float4 *>(a.v + base * DV + col);
+    if constexpr (FUSED) {
+      if (rg == 0) zz = *reinterpret_cast<const float4 *>(a.z + base * DV + col);
+      ga = a.a[base];
+      gb = a.b[base];
+    } else {
+      ga = a.g[base];
+      gb = a.beta[a.betaOff + base];
+    }
+  };
+  if (a.S) load_inputs(0);
+  float s[4][4];
+  const uint64_t sbase = (uint64_t)h * DK * DV;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (a.loadState && a.state_in) x = *reinterpret_cast<const float4 *>(a.state_in + sbase + (uint64_t)(r0 + i) * DV + col);
+    s[i][0] = x.x; s[i][1] = x.y; s[i][2] = x.z; s[i][3] = x.w;
+  }
+  const float qscale = 1.0f / sqrtf((float)DK);
+  const float an = FUSED ? a.a_neg[h] : 0.f, dtb = FUSED ? a.dt_bias[h] : 0.f;
+  float4 gam = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (FUSED && rg == 0) gam = *reinterpret_cast<const float4 *>(a.gamma + col);
+
+  // sum over the CTA's rows of per-thread partials p[4] for its 4 columns -> full sums, every thread
+  auto row_sum = [&](float (&p)[4], float (*red)[NC]) {
+#pragma unroll
+    for (int o = CG; o < 32; o <<= 1)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) p[c] += __shfl_xor_sync(0xffffffffu, p[c], o);
+    if (lane < CG) *reinterpret_cast<float4 *>(&red[warp][4 * lane]) = make_float4(p[0], p[1], p[2], p[3]);
+    __syncthreads();
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      const float4 x = *reinterpret_cast<const float4 *>(&red[w][4 * cg_]);
+      acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
+    }
+    p[0] = acc.x; p[1] = acc.y; p[2] = acc.z; p[3] = acc.w;
+  };
+
+  for (uint32_t t = 0; t < a.S; ++t) {
+    const uint64_t base = (uint64_t)(t + a.tOff) * a.H + h;
+    if (warp < 2) {  // l2norm(k), l2norm(q)/sqrt(dk)
+      float ss = kq[0] * kq[0] + kq[1] * kq[1] + kq[2] * kq[2] + kq[3] * kq[3];
+      ss = warp_sum(ss);
+      const float inv = (1.0f / sqrtf(ss + 1e-6f)) * (warp ? qscale : 1.0f);
+      *reinterpret_cast<float4 *>((warp ? qn_s : kn_s) + lane * 4) =
+          make_float4(kq[0] * inv, kq[1] * inv, kq[2] * inv, kq[3] * inv);
+    }
+    float gt, bt;
+    if constexpr (FUSED) {
+      gt = expf(an * softplus_stable(ga + dtb));
+      bt = sigmoidf_(gb);
+    } else {
+      gt = expf(ga);
+      bt = gb;
+    }
+    const float vt[4] = {vv.x, vv.y, vv.z, vv.w};
+    const float zt[4] = {zz.x, zz.y, zz.z, zz.w};
+    if (t + 1 < a.S) load_inputs(t + 1);
+    __syncthreads();
+    const float4 kn4 = *reinterpret_cast<const float4 *>(kn_s + r0);
+    const float4 qn4 = *reinterpret_cast<const float4 *>(qn_s + r0);
+    const float kn[4] = {kn4.x, kn4.y, kn4.z, kn4.w}, qn[4] = {qn4.x, qn4.y, qn4.z, qn4.w};
+    float kv[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        s[i][c] *= gt;
+        kv[c] = fmaf(s[i][c], kn[i], kv[c]);
+      }
+    row_sum(kv, red_kv);
+    float o[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const float delta = (vt[c] - kv[c]) * bt;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        s[i][c] = fmaf(kn[i], delta, s[i][c]);
+        o[c] = fmaf(s[i][c], qn[i], o[c]);
+      }
+    }
+    row_sum(o, red_o);
+    if constexpr (FUSED) {
+      if (t == 0) asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+      const int slot = t & 1;
+      if (warp == 0) {
+        float sq = lane < CG ? o[0] * o[0] + o[1] * o[1] + o[2] * o[2] + o[3] * o[3] : 0.f;
+        sq = warp_sum(sq);
+        if (lane == 0) mbar_expect_tx(&ss_bar[slot], 4 * kSplitCTAs);
+        if (lane < kSplitCTAs) {  // lane r stores this CTA's partial into rank r
+          uint32_t raddr, rbar;
+          asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(raddr) : "r"(smem_u32(&ss_in[slot][my_rank])), "r"(lane));
+          asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rbar) : "r"(smem_u32(&ss_bar[slot])), "r"(lane));
+          asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(raddr),
+                       "r"(__float_as_uint(sq)), "r"(rbar)
+                       : "memory");
+        }
+      }
+      if (rg == 0) {
+        float tot = 0.f;
+        if (mbar_wait(&ss_bar[slot], (t >> 1) & 1)) {
+#pragma unroll
+          for (int r = 0; r < kSplitCTAs; ++r) tot += ss_in[slot][r];
+        }
+        const float inv = 1.0f / sqrtf(tot / (float)DV + a.eps);
+        const float g4[4] = {gam.x, gam.y, gam.z, gam.w};
+        float y[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) y[c] = g4[c] * (o[c] * inv) * (zt[c] / (1.0f + expf(-zt[c])));
+        *reinterpret_cast<float4 *>(a.y + base * DV + col) = make_float4(y[0], y[1], y[2], y[3]);
+      }
+    }
+    if (rg == 0 && a.core) *reinterpret_cast<float4 *>(a.core + base * DV + col) = make_float4(o[0], o[1], o[2], o[3]);
+    // red_kv / red_o are rewritten by the next token only after its first block barrier
+  }
+  // A CTA leaves only after its threads of row group 0 received every peer's last partial, so no
+  // store into its shared memory is still on the way.  (S == 0: the startup barrier still pairs.)
+  if (FUSED && a.S == 0) asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+  if (a.state_out) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      *reinterpret_cast<float4 *>(a.state_out + sbase + (uint64_t)(r0 + i) * DV + col) =
+          make_float4(s[i][0], s[i][1], s[i][2], s[i][3]);
+  }
+}
+
+}  // namespace
+
+int poll_device_error_deltanet() {
+  int v = 0, z = 0;
+  if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)) != cudaSuccess) return BG_ELAUNCH;
+  if (v) cudaMemcpyToSymbol(g_device_error, &z, sizeof(int));
+  return v;
+}
+
+namespace {
+
 __global__ void gbeta_kernel(const float *a, const float *b, const float *an, const float *dt, uint32_t S, uint32_t H,
                              float *out) {
   const uint32_t n = S * H;
@@ -429,6 +625,33 @@ bool aligned16(const DeltaArgs &a) {
   return true;
 }
 
+// BGATTN_PDL=0 launches the decode kernel without programmatic dependent launch (A/B checks)
+bool pdl_enabled() {
+  static const bool v = [] {
+    const char *e = getenv("BGATTN_PDL");
+    return !(e && *e == '0');
+  }();
+  return v;
+}
+
+// columns per CTA of the split decode kernel: 16 (8-CTA clusters, default) or 32 (BGATTN_DN_COLS=32)
+int dn_split_cols() {
+  static const int v = [] {
+    const char *e = getenv("BGATTN_DN_COLS");
+    return (e && atoi(e) == 32) ? 32 : 16;
+  }();
+  return v;
+}
+
+// BGATTN_DN_SPLIT=0 keeps decode on the one-CTA-per-head vector kernel (A/B checks)
+bool dn_split_enabled() {
+  static const bool v = [] {
+    const char *e = getenv("BGATTN_DN_SPLIT");
+    return !(e && *e == '0');
+  }();
+  return v;
+}
+
 bool head_legacy() {
   static const bool v = [] {
     const char *e = getenv("BGATTN_DN_LEGACY");  // column-group kernel with the cluster norm (A/B)
@@ -445,6 +668,31 @@ int launch_dk(const DeltaArgs &a, cudaStream_t st) {
     // short calls (decode) take the vector layout; long recurrent runs keep the scalar one, whose
     // per-token reductions are four partials instead of sixteen
     const bool vec = a.S <= kVecMaxTokens && aligned16(a);
+    if (vec && dn_split_enabled()) {
+      const int nc = dn_split_cols();
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(128 / nc, a.H);
+      cfg.blockDim = dim3(nc * 8);
+      cfg.stream = st;
+      cudaLaunchAttribute attr[2];
+      int na = 0;
+      attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[na++].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+      if (fused) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = 128 / nc;
+        attr[na].val.clusterDim.y = 1;
+        attr[na++].val.clusterDim.z = 1;
+      }
+      cfg.attrs = attr;
+      cfg.numAttrs = na;
+      cudaError_t e;
+      if (nc == 32) e = fused ? cudaLaunchKernelEx(&cfg, deltanet_split_kernel<true, 32>, a)
+                              : cudaLaunchKernelEx(&cfg, deltanet_split_kernel<false, 32>, a);
+      else e = fused ? cudaLaunchKernelEx(&cfg, deltanet_split_kernel<true, 16>, a)
+                     : cudaLaunchKernelEx(&cfg, deltanet_split_kernel<false, 16>, a);
+      return e == cudaSuccess ? BG_OK : BG_ELAUNCH;
+    }
     if (vec && fused) deltanet_head_vec_kernel<true><<<a.H, 512, 0, st>>>(a);
     else if (vec) deltanet_head_vec_kernel<false><<<a.H, 512, 0, st>>>(a);
     else if (fused) deltanet_head_kernel<true><<<a.H, 512, 0, st>>>(a);
