@@ -21,7 +21,7 @@ EXPORTS = [
     "bg_gate_sigmoid", "bg_attention_noalloc", "bg_deltanet_chunked_workspace_size",
     "bg_deltanet_chunked", "bg_qk_norm_rope", "bg_conv1d_causal", "bg_slice_cols",
     "bg_kv_snapshot_bytes", "bg_kv_snapshot_save", "bg_kv_snapshot_restore", "bg_attention_noalloc_limit",
-    "bg_selftest_wait_expiry",
+    "bg_selftest_wait_expiry", "bg_kv_append_kv_pair",
 ]
 
 
@@ -58,6 +58,8 @@ _SIGS = {
     "bg_lse_merge": (C.c_int, [P, U32, U32, U32, P, P, U32, P]),
     "bg_kv_append": (C.c_int, [C.POINTER(KVCacheDesc), U32, U32, P, U32, U32, U32, U32, U32, P]),
     "bg_kv_append_kv": (C.c_int, [C.POINTER(KVCacheDesc), U32, P, P, U32, U32, U32, U32, U32, P]),
+    "bg_kv_append_kv_pair": (C.c_int, [C.POINTER(KVCacheDesc), C.POINTER(KVCacheDesc), U32, P, P, U32, U32, U32, U32,
+                                       U32, P]),
     "bg_qk_norm_rope": (C.c_int, [P, U32, U32, U32, U32, U32, U32, P, P, P, U32, U32, F, P,
                                   C.POINTER(KVCacheDesc), P]),
     "bg_conv1d_causal": (C.c_int, [P, P, P, U32, U32, U32, U32, P, P, P]),

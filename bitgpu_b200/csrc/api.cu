@@ -321,18 +321,38 @@ int bg_kv_append(const bg_kv_cache *kv, uint32_t which, uint32_t batch, const vo
                           pos0, (int)which, 1, (cudaStream_t)stream);
 }
 
-int bg_kv_append_kv(const bg_kv_cache *kv, uint32_t batch, const void *k_src, const void *v_src, uint32_t src_dtype,
-                    uint32_t S, uint32_t KV, uint32_t D, uint32_t pos0, bg_stream_t stream) {
-  if (!kv || !k_src || !v_src || src_dtype > BG_DT_F16 || !kv_mode_ok(kv->mode) || KV == 0) return BG_EINVAL;
-  if (!d_ok(D)) return BG_EUNSUPPORTED;
+// Validation shared by the K+V writers: the cache holds positions [pos0, pos0 + S) of this shape.
+static int check_append_kv(const bg_kv_cache *kv, uint32_t S, uint32_t D, uint32_t pos0) {
+  if (!kv || !kv_mode_ok(kv->mode)) return BG_EINVAL;
   if (kv->mode == BG_KV_Q8R && D % 128) return BG_EINVAL;
   if (!kv->K || !kv->V) return BG_EINVAL;
   if ((kv->mode == BG_KV_Q8 || kv->mode == BG_KV_Q8R) && (!kv->Ks || !kv->Vs)) return BG_EINVAL;
   const uint64_t cap = kv->window ? (uint64_t)kv->sinks + kv->window : kv->seq_stride;
   if ((uint64_t)pos0 + S > cap) return BG_EINVAL;
+  return BG_OK;
+}
+
+int bg_kv_append_kv(const bg_kv_cache *kv, uint32_t batch, const void *k_src, const void *v_src, uint32_t src_dtype,
+                    uint32_t S, uint32_t KV, uint32_t D, uint32_t pos0, bg_stream_t stream) {
+  if (!kv || !k_src || !v_src || src_dtype > BG_DT_F16 || KV == 0) return BG_EINVAL;
+  if (!d_ok(D)) return BG_EUNSUPPORTED;
+  if (int rc = check_append_kv(kv, S, D, pos0)) return rc;
   if (batch == 0 || S == 0) return BG_OK;
   return launch_kv_append(make_view(kv, KV, 0), (int)kv->mode, D, k_src, v_src, src_dtype == BG_DT_F16, batch, S,
                           pos0, 0, 2, (cudaStream_t)stream);
+}
+
+int bg_kv_append_kv_pair(const bg_kv_cache *kv0, const bg_kv_cache *kv1, uint32_t batch, const void *k_src,
+                         const void *v_src, uint32_t src_dtype, uint32_t S, uint32_t KV, uint32_t D, uint32_t pos0,
+                         bg_stream_t stream) {
+  if (!kv0 || !kv1 || !k_src || !v_src || src_dtype > BG_DT_F16 || KV == 0) return BG_EINVAL;
+  if (!d_ok(D)) return BG_EUNSUPPORTED;
+  if (int rc = check_append_kv(kv0, S, D, pos0)) return rc;
+  if (int rc = check_append_kv(kv1, S, D, pos0)) return rc;
+  if (batch == 0 || S == 0) return BG_OK;
+  const KVView v1 = make_view(kv1, KV, 0);
+  return launch_kv_append(make_view(kv0, KV, 0), (int)kv0->mode, D, k_src, v_src, src_dtype == BG_DT_F16, batch, S,
+                          pos0, 0, 2, (cudaStream_t)stream, &v1, (int)kv1->mode);
 }
 
 int bg_qk_norm_rope(const float *x, uint32_t batch, uint32_t S, uint32_t heads, uint32_t D, uint32_t x_stride,

@@ -6,7 +6,8 @@ namespace bg {
 
 // nsides 1: src0 -> K (first_v = 0) or V (first_v = 1); nsides 2: src0 -> K and src1 -> V.
 int launch_kv_append(const KVView &kv, int mode, uint32_t D, const void *src0, const void *src1, int src_f16,
-                     uint32_t B, uint32_t S, uint32_t pos0, int first_v, int nsides, cudaStream_t st);
+                     uint32_t B, uint32_t S, uint32_t pos0, int first_v, int nsides, cudaStream_t st,
+                     const KVView *kv2 = nullptr, int mode2 = 0);
 int launch_rmsnorm_rope(const float *x, uint32_t B, uint32_t R, uint32_t D, const float *gamma, const float *cosv,
                         const float *sinv, float eps, float *y, const KVView &kv, int mode, uint32_t pos, int to_cache,
                         cudaStream_t st);

@@ -20,14 +20,27 @@ __device__ __forceinline__ void store_row(void *data, float *scales, int mode, u
                                           const float (&x)[DPL]) {
   constexpr int D = DPL * 32;
   const uint64_t off = row * D + (uint64_t)lane * DPL;
+  // a lane's DPL values are contiguous: one vector store per lane (DPL = 2, 4, 8)
   if (mode == BG_KV_F32) {
     float *d = static_cast<float *>(data) + off;
+    if constexpr (DPL % 4 == 0) {
 #pragma unroll
-    for (int i = 0; i < DPL; ++i) d[i] = x[i];
+      for (int i = 0; i < DPL; i += 4) *reinterpret_cast<float4 *>(d + i) = make_float4(x[i], x[i + 1], x[i + 2], x[i + 3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < DPL; i += 2) *reinterpret_cast<float2 *>(d + i) = make_float2(x[i], x[i + 1]);
+    }
   } else if (mode == BG_KV_F16) {
     __half *d = static_cast<__half *>(data) + off;
+    uint32_t w[DPL / 2];
 #pragma unroll
-    for (int i = 0; i < DPL; i += 2) *reinterpret_cast<__half2 *>(d + i) = __floats2half2_rn(x[i], x[i + 1]);
+    for (int i = 0; i < DPL; i += 2) {
+      __half2 hv = __floats2half2_rn(x[i], x[i + 1]);
+      w[i / 2] = *reinterpret_cast<uint32_t *>(&hv);
+    }
+    if constexpr (DPL == 8) *reinterpret_cast<uint4 *>(d) = make_uint4(w[0], w[1], w[2], w[3]);
+    else if constexpr (DPL == 4) *reinterpret_cast<uint2 *>(d) = make_uint2(w[0], w[1]);
+    else *reinterpret_cast<uint32_t *>(d) = w[0];
   } else if (mode == BG_KV_Q8) {
     // per 32-element block: s = max(absmax, 1e-30) (copy_kv8.wgsl:30-35)
     float am = 0.f;
@@ -38,8 +51,12 @@ __device__ __forceinline__ void store_row(void *data, float *scales, int mode, u
     for (int o = LPB / 2; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
     const float s = fmaxf(am, 1e-30f);
     int8_t *d = static_cast<int8_t *>(data) + off;
+    uint32_t w[(DPL + 3) / 4] = {};
 #pragma unroll
-    for (int i = 0; i < DPL; ++i) d[i] = snorm8_encode(x[i], s);
+    for (int i = 0; i < DPL; ++i) w[i / 4] |= (uint32_t)(uint8_t)snorm8_encode(x[i], s) << (8 * (i % 4));
+    if constexpr (DPL == 8) *reinterpret_cast<uint2 *>(d) = make_uint2(w[0], w[1]);
+    else if constexpr (DPL == 4) *reinterpret_cast<uint32_t *>(d) = w[0];
+    else *reinterpret_cast<uint16_t *>(d) = (uint16_t)w[0];
     if ((lane % LPB) == 0) scales[row * (D / 32) + (lane * DPL) / 32] = s;
   } else {  // BG_KV_Q8R: absmax/127 per 128 values, round-half-even
     float am = 0.f;
@@ -62,10 +79,11 @@ __device__ __forceinline__ void store_row(void *data, float *scales, int mode, u
 }
 
 // Rows [side][b][s][kv]: side 0 writes src0 into the cache's `first_v ? V : K`, side 1 (when
-// nsides == 2) writes src1 into V.
+// nsides == 2) writes src1 into V.  With kv2.K != nullptr the same rows also go into a second cache
+// (its own codec), read from the source once.
 template <int DPL>
-__global__ void kv_append_kernel(KVView kv, int mode, const void *src0, const void *src1, int src_f16, uint32_t B,
-                                 uint32_t S, uint32_t pos0, int first_v, int nsides) {
+__global__ void kv_append_kernel(KVView kv, int mode, KVView kv2, int mode2, const void *src0, const void *src1,
+                                 int src_f16, uint32_t B, uint32_t S, uint32_t pos0, int first_v, int nsides) {
   constexpr int D = DPL * 32;
   const uint32_t gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -80,6 +98,11 @@ __global__ void kv_append_kernel(KVView kv, int mode, const void *src0, const vo
   const uint64_t row = cache_row(kv, b, pos0 + s, kvh);
   store_row<DPL>(const_cast<void *>(to_v ? kv.V : kv.K), const_cast<float *>(to_v ? kv.Vs : kv.Ks), mode, row, lane,
                  x);
+  if (kv2.K) {
+    const uint64_t row2 = cache_row(kv2, b, pos0 + s, kvh);
+    store_row<DPL>(const_cast<void *>(to_v ? kv2.V : kv2.K), const_cast<float *>(to_v ? kv2.Vs : kv2.Ks), mode2, row2,
+                   lane, x);
+  }
 }
 
 // rmsnorm_rope_sg.wgsl:21-33 (+ the _kv8 write side): y = (x*inv*gamma) rotated by cos/sin.
@@ -196,22 +219,26 @@ __global__ void qk_norm_rope_kernel(const float *x, uint32_t B, uint32_t S, uint
 }
 
 template <int DPL>
-int launch_append_d(const KVView &kv, int mode, const void *src0, const void *src1, int f16, uint32_t B, uint32_t S,
-                    uint32_t pos0, int first_v, int nsides, cudaStream_t st) {
+int launch_append_d(const KVView &kv, int mode, const KVView &kv2, int mode2, const void *src0, const void *src1,
+                    int f16, uint32_t B, uint32_t S, uint32_t pos0, int first_v, int nsides, cudaStream_t st) {
   const uint64_t warps = (uint64_t)B * S * kv.KV * nsides;
   const uint32_t blocks = (uint32_t)((warps * 32 + 255) / 256);
-  kv_append_kernel<DPL><<<blocks, 256, 0, st>>>(kv, mode, src0, src1, f16, B, S, pos0, first_v, nsides);
+  kv_append_kernel<DPL><<<blocks, 256, 0, st>>>(kv, mode, kv2, mode2, src0, src1, f16, B, S, pos0, first_v, nsides);
   return cudaGetLastError() == cudaSuccess ? BG_OK : BG_ELAUNCH;
 }
 
 }  // namespace
 
 int launch_kv_append(const KVView &kv, int mode, uint32_t D, const void *src0, const void *src1, int src_f16,
-                     uint32_t B, uint32_t S, uint32_t pos0, int first_v, int nsides, cudaStream_t st) {
+                     uint32_t B, uint32_t S, uint32_t pos0, int first_v, int nsides, cudaStream_t st,
+                     const KVView *kv2, int mode2) {
+  KVView none = kv;
+  none.K = none.V = nullptr;
+  const KVView &k2 = kv2 ? *kv2 : none;
   switch (D) {
-    case 64: return launch_append_d<2>(kv, mode, src0, src1, src_f16, B, S, pos0, first_v, nsides, st);
-    case 128: return launch_append_d<4>(kv, mode, src0, src1, src_f16, B, S, pos0, first_v, nsides, st);
-    case 256: return launch_append_d<8>(kv, mode, src0, src1, src_f16, B, S, pos0, first_v, nsides, st);
+    case 64: return launch_append_d<2>(kv, mode, k2, mode2, src0, src1, src_f16, B, S, pos0, first_v, nsides, st);
+    case 128: return launch_append_d<4>(kv, mode, k2, mode2, src0, src1, src_f16, B, S, pos0, first_v, nsides, st);
+    case 256: return launch_append_d<8>(kv, mode, k2, mode2, src0, src1, src_f16, B, S, pos0, first_v, nsides, st);
     default: return BG_EUNSUPPORTED;
   }
 }

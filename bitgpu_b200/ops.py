@@ -108,6 +108,17 @@ class KVCache:
         check("bg_kv_append_kv", lib().bg_kv_append_kv(C.byref(d), B, _p(k), _p(v), _DT[k.dtype], S, KV, D, pos0,
                                                         _stream()))
 
+    def append_kv_pair(self, other, k, v, pos0):
+        """``append_kv`` into this cache and ``other`` (same shape, any codec) in one pass."""
+        _need(k, name="k")
+        _need(v, k.dtype, "v")
+        if k.shape != v.shape:
+            raise ValueError("k and v shapes differ")
+        B, S, KV, D = k.shape
+        d0, d1 = self.desc(), other.desc()
+        check("bg_kv_append_kv_pair", lib().bg_kv_append_kv_pair(C.byref(d0), C.byref(d1), B, _p(k), _p(v),
+                                                                  _DT[k.dtype], S, KV, D, pos0, _stream()))
+
     def write_normed_k(self, x, gamma, eps, pos, cos=None, sin=None, y=None):
         """Fused K path of the decode step (``rmsnorm_rope_sg{,_kv16,_kv8}``, engine.ts:1533-1540):
         ``x[batch, KV, D]`` -> RMSNorm*gamma -> RoPE(cos, sin of this position; None = unroped)

@@ -146,6 +146,15 @@ int bg_kv_append_kv(const bg_kv_cache *kv, uint32_t batch, const void *k_src, co
                     uint32_t src_dtype, uint32_t S, uint32_t KV, uint32_t D, uint32_t pos0,
                     bg_stream_t stream);
 
+/* bg_kv_append_kv_pair: the same K and V rows written into two caches of one shape in a single
+ * pass that reads the source once (e.g. a prefill's rows into an f16 cache and a q8 cache, the
+ * BASELINE config-3 write); each cache keeps its own codec.  Same layout and errors as
+ * bg_kv_append_kv on each cache.  No single reference dispatch does this: it replaces two
+ * appendKV steps (engine.ts:1385-1393) over different caches. */
+int bg_kv_append_kv_pair(const bg_kv_cache *kv0, const bg_kv_cache *kv1, uint32_t batch,
+                         const void *k_src, const void *v_src, uint32_t src_dtype, uint32_t S,
+                         uint32_t KV, uint32_t D, uint32_t pos0, bg_stream_t stream);
+
 /* bg_qk_norm_rope: the gated-attention prologue of engine.ts:1471-1485 in one launch, for
  * batch x S x heads head rows of width D:
  *   split_head.wgsl  row (b, s, h) is read at x + ((b*S + s)*heads + h)*x_stride + x_off

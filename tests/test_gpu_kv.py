@@ -159,3 +159,27 @@ def test_roll_stream_vs_oracle(ops):
             exp = OA.attend(q[0], OA.rotate_keys_at_read(Kl, c, s), Vl, fill - 1)
             ok, mad, cos_ = gate_ok(out[0].cpu().numpy(), exp)
             assert ok, (step, mad, cos_)
+
+
+@pytest.mark.parametrize("D", [64, 128, 256])
+@pytest.mark.parametrize("modes", [("f16", "q8"), ("f32", "q8r"), ("q8", "f16")])
+def test_append_kv_pair_equals_two_appends(ops, D, modes):
+    """bg_kv_append_kv_pair writes the same bytes as one bg_kv_append_kv per cache (codecs, scales,
+    a ring cache's wrap and an f16 source included)."""
+    if "q8r" in modes and D % 128:
+        pytest.skip("q8r needs head_dim % 128")
+    B, S, KV, pos0 = 3, 37, 4, 11
+    g = torch.Generator(device="cuda").manual_seed(D)
+    k = torch.randn((B, S, KV, D), generator=g, device="cuda").half()
+    v = torch.randn((B, S, KV, D), generator=g, device="cuda").half()
+    mk = lambda m: ops.KVCache(B, 0, KV, D, mode=m, sinks=4, window=60)
+    a0, a1, b0, b1 = mk(modes[0]), mk(modes[1]), mk(modes[0]), mk(modes[1])
+    for c in (a0, a1, b0, b1):
+        c.ring_head = 50
+    a0.append_kv_pair(a1, k, v, pos0)
+    b0.append_kv(k, v, pos0)
+    b1.append_kv(k, v, pos0)
+    for x, y in ((a0, b0), (a1, b1)):
+        assert torch.equal(x.K, y.K) and torch.equal(x.V, y.V)
+        if x.Ks is not None:
+            assert torch.equal(x.Ks, y.Ks) and torch.equal(x.Vs, y.Vs)
