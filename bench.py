@@ -356,7 +356,8 @@ GA_H, GA_KV, GA_D, GA_L = 24, 4, 256, 131072
 
 def run_gated(torch, ops, args, ws, rank, barrier, max_over_ranks):
     """Config 5b: one stream's gated head_dim-256 decode at 131072 positions, the cache split over
-    the ranks (bitgpu_b200.splitkv: partials + NCCL all-gather + LSE merge with the gate fused)."""
+    the ranks (bitgpu_b200.splitkv: split-KV partials pushed into every rank over NVLink, merge with
+    the gate fused; the NCCL all-gather form timed beside it)."""
     from bitgpu_b200.splitkv import SplitKVDecoder
     L = args.gated_ctx
     dec = SplitKVDecoder(L)
@@ -371,21 +372,50 @@ def run_gated(torch, ops, args, ws, rank, barrier, max_over_ranks):
     q = torch.randn((1, 1, GA_H, GA_D), generator=gq, device="cuda")
     gate = torch.randn((1, 1, GA_H, GA_D), generator=gq, device="cuda")
     scale = 1.0 / GA_D ** 0.5
+    byts = 2 * L * GA_KV * GA_D * 2 + 3 * GA_H * GA_D * 4
     if ws == 1:
         out = torch.empty_like(q)
         fn = lambda: ops.attention(q, cache, L - 1, scale=scale, gate=gate, out=out)
         launches = 1
     else:
-        # the whole step -- partials kernel, NCCL all-gather, merge kernel -- replayed as one CUDA
-        # graph, so the host adds nothing per step
+        # the whole step -- split-KV kernel, push of the rows into every rank's gather buffer over
+        # NVLink, merge -- replayed as one CUDA graph, so the host adds nothing per step
         fn = ops.Graphed(lambda: dec.step(q, cache, L - 1, gate=gate, scale=scale))
-        launches = 2
+        launches = 3
     ms = max_over_ranks(time_steps(torch, fn, args.steps, args.warmup, barrier))
-    byts = 2 * L * GA_KV * GA_D * 2 + 3 * GA_H * GA_D * 4
-    del cache
-    torch.cuda.empty_cache()
-    return {"ms": ms, "bytes": byts, "gbs": byts / (ms * 1e-3) / 1e9, "launches_per_step": launches,
-            "nccl_bytes_per_rank": 0 if ws == 1 else GA_H * (GA_D + 2) * 4}
+    res = {"ms": ms, "bytes": byts, "gbs": byts / (ms * 1e-3) / 1e9, "launches_per_step": launches,
+           "exchange": dec.exchange if ws > 1 else None,
+           "exchange_bytes_per_rank": 0 if ws == 1 else GA_H * (GA_D + 2) * 4 * ws}
+    if ws > 1:
+        # the same step with the NCCL all-gather exchange (A/B)
+        dn = SplitKVDecoder(L, exchange="nccl")
+        fn2 = ops.Graphed(lambda: dn.step(q, cache, L - 1, gate=gate, scale=scale))
+        res["nccl_ms"] = max_over_ranks(time_steps(torch, fn2, args.steps, args.warmup, barrier))
+        # strong scaling of this config: the whole 131072-position step on one GPU (rank 0)
+        del cache
+        torch.cuda.empty_cache()
+        one = 0.0
+        if rank == 0:
+            full = ops.KVCache(1, L, GA_KV, GA_D, mode="f16", device="cuda")
+            for p0 in range(0, L, 8192):
+                m = min(8192, L - p0)
+                for w in (0, 1):
+                    full.append(w, torch.randn((1, m, GA_KV, GA_D), generator=g, device="cuda"), p0)
+            out1 = torch.empty_like(q)
+            one = time_steps(torch, lambda: ops.attention(q, full, L - 1, scale=scale, gate=gate, out=out1),
+                             args.steps, args.warmup, lambda: None)
+            del full
+            torch.cuda.empty_cache()
+        barrier()
+        res["ms_1gpu"] = max_over_ranks(one)
+        res["strong_scaling_efficiency"] = res["ms_1gpu"] / (ws * ms)
+        del fn, fn2
+        dec.close()
+        dn.close()
+    else:
+        del cache
+        torch.cuda.empty_cache()
+    return res
 
 
 # config 5a; 27B hybrid linear layer: 16 key heads, 48 value heads, 128 x 128
@@ -561,7 +591,11 @@ def run_ours(args):
                           hbm_roof(r["gbs"] / ws, "per-GPU share of the step's algorithmic bytes / step time"),
                           r["launches_per_step"] * args.steps, clk.stop())
         line["scaling"] = "strong"
-        line["nccl_bytes_per_rank_per_step"] = r["nccl_bytes_per_rank"]
+        line["exchange"] = r["exchange"]
+        line["exchange_bytes_per_rank_per_step"] = r["exchange_bytes_per_rank"]
+        for k in ("nccl_ms", "ms_1gpu", "strong_scaling_efficiency"):
+            if k in r:
+                line[k] = round(r[k], 4)
         return finish(line)
     if args.workload == "deltanet":
         clk = Clocks(local)
@@ -666,7 +700,15 @@ def run_ours(args):
         r = run_gated(torch, ops, gs, ws, rank, barrier, max_over_ranks)
         extra["gated_d256"] = {"metric": "config 5b gated decode GB/s (split-KV over the GPUs)",
                                "value": round(r["gbs"], 1), "unit": "GB/s", "ms_per_step": round(r["ms"], 4),
-                               "frac": round(r["gbs"] / ws / hbm, 4), "scaling": "strong"}
+                               "frac": round(r["gbs"] / ws / hbm, 4), "scaling": "strong",
+                               "exchange": r["exchange"]}
+        for k in ("nccl_ms", "ms_1gpu", "strong_scaling_efficiency"):
+            if k in r:
+                extra["gated_d256"][k] = round(r[k], 4)
+        if "strong_scaling_efficiency" in r:
+            extra_top = {"gated_d256_strong_scaling_efficiency": round(r["strong_scaling_efficiency"], 4)}
+        else:
+            extra_top = {}
     if "deltanet" in variants:
         r = run_deltanet(torch, ops, short, rank, barrier, max_over_ranks)
         extra["deltanet"] = {"metric": "config 5a DeltaNet decode GB/s (per GPU, replicas)",
@@ -701,6 +743,8 @@ def run_ours(args):
                             "frac": round(r["per_gpu_gbs"] / hbm, 4), "bytes_per_step_per_gpu": r["bytes"]}
                         for m, r in results.items() if m != modes[0]}
     line["variants"].update(extra)
+    if "gated" in variants:
+        line.update(extra_top)
     if "e2e" in head:
         line["e2e"] = head["e2e"]
     if ws == 1 and not args.no_cpu_baseline:

@@ -21,7 +21,8 @@ EXPORTS = [
     "bg_gate_sigmoid", "bg_attention_noalloc", "bg_deltanet_chunked_workspace_size",
     "bg_deltanet_chunked", "bg_qk_norm_rope", "bg_conv1d_causal", "bg_slice_cols",
     "bg_kv_snapshot_bytes", "bg_kv_snapshot_save", "bg_kv_snapshot_restore", "bg_attention_noalloc_limit",
-    "bg_selftest_wait_expiry", "bg_kv_append_kv_pair",
+    "bg_selftest_wait_expiry", "bg_kv_append_kv_pair", "bg_peer_exchange_bytes", "bg_peer_exchange_flags_offset",
+    "bg_attention_partials_peer_workspace_size", "bg_attention_partials_peer", "bg_lse_merge_peer",
 ]
 
 
@@ -34,6 +35,15 @@ class KVCacheDesc(C.Structure):
     _fields_ = [("K", C.c_void_p), ("V", C.c_void_p), ("Ks", C.c_void_p), ("Vs", C.c_void_p),
                 ("seq_stride", C.c_uint64), ("mode", C.c_uint32), ("sinks", C.c_uint32),
                 ("window", C.c_uint32), ("ring_head", C.c_uint32)]
+
+
+MAX_PEERS = 8
+
+
+class PeerExchange(C.Structure):
+    _fields_ = [("nranks", C.c_uint32), ("rank", C.c_uint32), ("gather", C.c_void_p * MAX_PEERS),
+                ("flags", C.c_void_p * MAX_PEERS), ("step", C.c_void_p), ("done", C.c_void_p),
+                ("spin_limit", C.c_uint32)]
 
 
 class BgError(RuntimeError):
@@ -78,6 +88,12 @@ _SIGS = {
     "bg_deltanet_chunked_workspace_size": (SZ, [U32, U32, U32, U32]),
     "bg_deltanet_chunked": (C.c_int, [U32, U32, U32, U32, U32, P, P, P, P, P, P, P, P, P, F, P, P, P, P, P, SZ, P]),
     "bg_attention_noalloc_limit": (SZ, []),
+    "bg_peer_exchange_bytes": (SZ, [U32, U32, U32]),
+    "bg_peer_exchange_flags_offset": (SZ, [U32, U32, U32]),
+    "bg_attention_partials_peer_workspace_size": (SZ, [C.POINTER(AttnParams), U32]),
+    "bg_attention_partials_peer": (C.c_int, [C.POINTER(AttnParams), U32, P, U32, C.POINTER(KVCacheDesc), P, P, F, U32,
+                                             U32, C.POINTER(PeerExchange), P, SZ, P]),
+    "bg_lse_merge_peer": (C.c_int, [C.POINTER(PeerExchange), U32, U32, P, P, U32, P]),
     "bg_selftest_wait_expiry": (C.c_int, [U32, P]),
     "bg_attention_noalloc": (C.c_int, [C.POINTER(AttnParams), U32, P, U32, C.POINTER(KVCacheDesc), P, P, F, P, P,
                                        U32, P]),

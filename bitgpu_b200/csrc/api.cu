@@ -64,11 +64,11 @@ size_t part_bytes(uint32_t nsplit, uint64_t rows, uint32_t D) { return (size_t)n
 int run_attention(const bg_attn_params *p, uint32_t batch, const void *q, uint32_t q_dtype, const bg_kv_cache *kv,
                   const float *cosT, const float *sinT, float scale, uint32_t pos_lo, uint32_t pos_hi,
                   uint32_t row_offset, float *partials_out, const float *gate, void *out, uint32_t out_dtype,
-                  void *ws, size_t ws_bytes, cudaStream_t st) {
+                  void *ws, size_t ws_bytes, cudaStream_t st, const bg_peer_exchange *peer = nullptr) {
   const float sc = scale > 0.f ? scale : 1.0f / sqrtf((float)p->D);
   // dense prefill on the tensor cores (f16 / f32 queries over an f16 or q8 cache, or an f32 cache
   // in 3xTF32; whole causal range, optional sigmoid gate)
-  if (!partials_out && !g_force_generic &&
+  if (!partials_out && !peer && !g_force_generic &&
       prefill_tc_supported((int)kv->mode, p->D, p->S, cosT != nullptr, kv->window != 0)) {
     PrefillArgs pa;
     pa.q = q;
@@ -119,6 +119,7 @@ int run_attention(const bg_attn_params *p, uint32_t batch, const void *q, uint32
                                                         kv->window != 0);
   a.nsplit = attn_num_splits(batch, p->S, p->H, p->KV, p->D, L, a.mode, tc, cosT != nullptr);
   if (const uint32_t ov = env_nsplit()) a.nsplit = ov;
+  if (peer && a.nsplit < 2) a.nsplit = 2;  // the push kernel merges at least two local splits
   a.chunk = ((L + a.nsplit - 1) / a.nsplit + 63) / 64 * 64;  // whole 64-position tiles
   if (a.nsplit == 1) {
     // one split: the kernel writes the final rows (or the caller's partial rows) itself
@@ -137,6 +138,7 @@ int run_attention(const bg_attn_params *p, uint32_t batch, const void *q, uint32
   int rc = tc ? launch_attn_tc(a, st) : BG_EUNSUPPORTED;
   if (rc == BG_EUNSUPPORTED) rc = launch_attn_generic(a, st);
   if (rc || a.nsplit == 1) return rc;
+  if (peer) return launch_lse_push(a.partials, a.nsplit, (uint32_t)rows, p->D, peer, st);
   if (partials_out) return launch_lse_merge(a.partials, a.nsplit, (uint32_t)rows, p->D, nullptr, partials_out, -1, st);
   return launch_lse_merge(a.partials, a.nsplit, (uint32_t)rows, p->D, gate, out, out_dtype == BG_DT_F16, st);
 }
@@ -255,6 +257,7 @@ int bg_device_status(bg_stream_t stream) {
   if (!e) e = poll_device_error_selftest();
   if (!e) e = poll_device_error_prefill_tf32();
   if (!e) e = poll_device_error_deltanet();
+  if (!e) e = poll_device_error_peer();
   return e ? (e < 0 ? e : BG_ELAUNCH) : BG_OK;
 }
 
@@ -305,6 +308,58 @@ int bg_lse_merge(const float *partials, uint32_t nsplit, uint32_t rows, uint32_t
                  uint32_t out_dtype, bg_stream_t stream) {
   if (!partials || !out || nsplit == 0 || D == 0 || out_dtype > BG_DT_F16) return BG_EINVAL;
   return launch_lse_merge(partials, nsplit, rows, D, gate, out, out_dtype == BG_DT_F16, (cudaStream_t)stream);
+}
+
+static int check_peer(const bg_peer_exchange *x) {
+  if (!x || x->nranks == 0 || x->nranks > BG_MAX_PEERS || x->rank >= x->nranks || !x->step || !x->done)
+    return BG_EINVAL;
+  for (uint32_t r = 0; r < x->nranks; ++r)
+    if (!x->gather[r] || !x->flags[r]) return BG_EINVAL;
+  return BG_OK;
+}
+
+size_t bg_peer_exchange_flags_offset(uint32_t nranks, uint32_t rows, uint32_t D) {
+  const size_t g = (size_t)2 * nranks * rows * (D + 2) * sizeof(float);
+  return (g + 255) / 256 * 256;
+}
+
+size_t bg_peer_exchange_bytes(uint32_t nranks, uint32_t rows, uint32_t D) {
+  return bg_peer_exchange_flags_offset(nranks, rows, D) + ((size_t)nranks * sizeof(uint32_t) + 255) / 256 * 256;
+}
+
+size_t bg_attention_partials_peer_workspace_size(const bg_attn_params *p, uint32_t batch) {
+  if (!p || !p->KV || !p->H) return 0;
+  const size_t two = part_bytes(2, (uint64_t)batch * p->S * p->H, p->D);
+  const size_t ws = attention_split_workspace_bytes(p, batch);
+  return ws > two ? ws : two;
+}
+
+int bg_attention_partials_peer(const bg_attn_params *p, uint32_t batch, const void *q, uint32_t q_dtype,
+                               const bg_kv_cache *kv, const float *cosT, const float *sinT, float scale,
+                               uint32_t pos_lo, uint32_t pos_hi, const bg_peer_exchange *x, void *workspace,
+                               size_t workspace_bytes, bg_stream_t stream) {
+  if (int rc = check_peer(x)) return rc;
+  if (!p || !kv || !q || q_dtype > BG_DT_F16) return BG_EINVAL;
+  if (p->H == 0 || p->KV == 0 || p->H % p->KV || !kv_mode_ok(kv->mode)) return BG_EINVAL;
+  if (!d_ok(p->D)) return BG_EUNSUPPORTED;
+  if (p->Ltot != p->posBase + p->S || pos_lo > pos_hi || pos_hi > p->Ltot) return BG_EINVAL;
+  if (kv->window) return BG_EUNSUPPORTED;
+  if (pos_hi - pos_lo > kv->seq_stride) return BG_EINVAL;
+  if ((cosT == nullptr) != (sinT == nullptr)) return BG_EINVAL;
+  if (batch == 0 || p->S == 0) return BG_OK;
+  // the other ranks wait for this rank's rows every step, also when its slice attends nothing
+  if (pos_hi == pos_lo) return launch_lse_push(nullptr, 0, batch * p->S * p->H, p->D, x, (cudaStream_t)stream);
+  return run_attention(p, batch, q, q_dtype, kv, cosT, sinT, scale, pos_lo, pos_hi, pos_lo, nullptr, nullptr, nullptr,
+                       0, workspace, workspace_bytes, (cudaStream_t)stream, x);
+}
+
+int bg_lse_merge_peer(const bg_peer_exchange *x, uint32_t rows, uint32_t D, const float *gate, void *out,
+                      uint32_t out_dtype, bg_stream_t stream) {
+  int rc = check_peer(x);
+  if (rc) return rc;
+  if (!out || out_dtype > BG_DT_F16) return BG_EINVAL;
+  if (rows == 0) return BG_OK;
+  return launch_lse_merge_peer(x, rows, D, gate, out, out_dtype == BG_DT_F16, (cudaStream_t)stream);
 }
 
 int bg_kv_append(const bg_kv_cache *kv, uint32_t which, uint32_t batch, const void *src, uint32_t src_dtype,

@@ -48,6 +48,11 @@ bool roll_legacy();  // BGATTN_ROLL_LEGACY=1 selects the one-head-per-CTA kernel
 int poll_device_error_attn_tc();
 // Split-KV partial scratch a bg_attention call may need (the part every kernel path shares).
 size_t attention_split_workspace_bytes(const bg_attn_params *p, uint32_t batch);
+int launch_lse_push(const float *partials, uint32_t nsplit, uint32_t rows, uint32_t D, const bg_peer_exchange *x,
+                    cudaStream_t st);
+int launch_lse_merge_peer(const bg_peer_exchange *x, uint32_t rows, uint32_t D, const float *gate, void *out,
+                          int out_f16, cudaStream_t st);
+int poll_device_error_peer();
 int poll_device_error_attn_roll();
 
 }  // namespace bg

@@ -5,16 +5,25 @@ The reference is single-device; this is the B200 extension for a stream whose ca
 over the ranks of one node.  Rank r holds the contiguous slice of cache positions
 ``[lo_r, hi_r)`` (``split_bounds``).  Every step:
 
-1. each rank runs ``bg_attention_partials`` over its slice and produces rows of
+1. each rank runs the split-KV partials over its slice and produces rows of
    ``(unnormalised o[D], m, l)``;
-2. one NCCL all-gather over NVLink brings every rank's partial rows into local memory;
-3. every rank merges the partials by log-sum-exp with ``bg_lse_merge``, with the sigmoid output
-   gate fused into the merge.
+2. the rows reach every rank;
+3. every rank merges the partials by log-sum-exp, with the sigmoid output gate fused into the
+   merge.
 
-The payload is ``H*(D+2)*4`` bytes per rank per query row (24.8 KB for 24 heads of 256).  No kernel
-reads peer memory.
+Step 2 has two forms:
 
-``partials_fn`` / ``merge_fn`` default to the CUDA entry points.  The CPU tests substitute the
+* ``exchange="peer"`` (default on GPUs): ``bg_attention_partials_peer`` stores the rows straight
+  into every rank's gather buffer over NVLink (plain peer stores into torch symmetric memory) and
+  raises per-source arrival counters; ``bg_lse_merge_peer`` waits for them with a bounded spin,
+  merges and gates.  Two kernels per step, no collective; the step counter lives on the device,
+  so a step can be captured in a CUDA graph.
+* ``exchange="nccl"``: ``bg_attention_partials``, one NCCL all-gather, ``bg_lse_merge`` (also the
+  form the CPU tests run on ``gloo`` ranks).
+
+The payload is ``H*(D+2)*4`` bytes per rank per query row (24.8 KB for 24 heads of 256).
+
+``partials_fn`` / ``merge_fn`` replace the kernels of the ``nccl`` form: the CPU tests substitute the
 oracle, so the collective orchestration runs on ``gloo`` ranks without a GPU.
 """
 import torch
@@ -26,6 +35,42 @@ class PeerFailure(RuntimeError):
     the step) and the collective ended with an error or ran into the process group's timeout.
     The surviving ranks raise this instead of waiting forever; the stream's output for that step
     does not exist."""
+
+
+class PeerExchange:
+    """One rank's side of the peer-memory exchange: a buffer every rank of ``group`` can address
+    (torch symmetric memory: gather slots ``[2][nranks][rows][D+2]`` f32, then ``nranks`` u32
+    arrival counters), this rank's step / merge counters, and the ``bg_peer_exchange`` descriptor
+    that carries every rank's addresses as seen from this GPU."""
+
+    def __init__(self, rows, D, group=None, spin_limit=0):
+        import torch.distributed._symmetric_memory as symm_mem
+        from ._lib import MAX_PEERS, PeerExchange as Desc, lib
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > MAX_PEERS:
+            raise ValueError(f"peer exchange supports at most {MAX_PEERS} ranks")
+        self.rows, self.D = rows, D
+        L = lib()
+        nbytes = L.bg_peer_exchange_bytes(self.world, rows, D)
+        foff = L.bg_peer_exchange_flags_offset(self.world, rows, D)
+        dev = torch.device("cuda", torch.cuda.current_device())
+        gname = (group or dist.group.WORLD).group_name
+        self.buf = symm_mem.empty(nbytes, dtype=torch.uint8, device=dev)
+        self.buf.zero_()
+        self.handle = symm_mem.rendezvous(self.buf, gname)
+        self.ctr = torch.zeros(2, dtype=torch.int32, device=dev)  # step, done
+        ptrs = list(self.handle.buffer_ptrs)
+        self.desc = Desc()
+        self.desc.nranks, self.desc.rank = self.world, self.rank
+        for r in range(self.world):
+            self.desc.gather[r] = ptrs[r]
+            self.desc.flags[r] = ptrs[r] + foff
+        self.desc.step = self.ctr.data_ptr()
+        self.desc.done = self.ctr.data_ptr() + 4
+        self.desc.spin_limit = spin_limit
+        torch.cuda.synchronize()
+        dist.barrier(group)  # every rank's buffer is zeroed before anyone pushes
 
 
 def split_bounds(L, world):
@@ -53,7 +98,7 @@ def _cuda_merge(gathered, out_shape, gate):
 class SplitKVDecoder:
     """One rank's view of a stream whose KV positions are sharded over ``group``."""
 
-    def __init__(self, L, group=None, partials_fn=None, merge_fn=None):
+    def __init__(self, L, group=None, partials_fn=None, merge_fn=None, exchange="auto", spin_limit=0):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -61,12 +106,35 @@ class SplitKVDecoder:
         self.lo, self.hi = self.bounds[self.rank]
         self.partials_fn = partials_fn or _cuda_partials
         self.merge_fn = merge_fn or _cuda_merge
+        if exchange == "auto":
+            exchange = "peer" if (self.world > 1 and partials_fn is None and merge_fn is None
+                                  and dist.get_backend(group) == "nccl") else "nccl"
+        if exchange not in ("peer", "nccl"):
+            raise ValueError(exchange)
+        self.exchange = exchange
+        self.spin_limit = spin_limit
+        self.px = None
+
+    def close(self):
+        """Release the peer buffers collectively (every rank calls it, with no step in flight)
+        before the process group goes away."""
+        if self.px is not None:
+            torch.cuda.synchronize()
+            dist.barrier(self.group)
+            self.px = None
 
     def step(self, q, local_cache, pos_base, gate=None, scale=0.0):
         """``q[B, S, H, D]`` (replicated on every rank) -> gated attention output ``[B, S, H, D]``
         over all ranks' positions ``0 .. pos_base+qi``."""
         B, S, H, D = q.shape
         hi = max(self.lo, min(self.hi, pos_base + S))  # a slice past the last position is empty
+        if self.exchange == "peer" and self.world > 1:
+            from . import ops
+            rows = B * S * H
+            if self.px is None or (self.px.rows, self.px.D) != (rows, D):
+                self.px = PeerExchange(rows, D, self.group, self.spin_limit)
+            ops.attention_partials_peer(q, local_cache, pos_base, self.lo, hi, self.px, scale=scale)
+            return ops.lse_merge_peer(self.px, (B, S, H, D), gate=gate)
         part = self.partials_fn(q, local_cache, pos_base, self.lo, hi, scale)
         if self.world == 1:
             gathered = part.unsqueeze(0)
