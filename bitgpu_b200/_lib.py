@@ -22,7 +22,7 @@ EXPORTS = [
     "bg_deltanet_chunked", "bg_qk_norm_rope", "bg_conv1d_causal", "bg_slice_cols",
     "bg_kv_snapshot_bytes", "bg_kv_snapshot_save", "bg_kv_snapshot_restore", "bg_attention_noalloc_limit",
     "bg_selftest_wait_expiry", "bg_kv_append_kv_pair", "bg_peer_exchange_bytes", "bg_peer_exchange_flags_offset",
-    "bg_attention_partials_peer_workspace_size", "bg_attention_partials_peer", "bg_lse_merge_peer",
+    "bg_attention_peer_workspace_size", "bg_attention_peer",
 ]
 
 
@@ -43,7 +43,7 @@ MAX_PEERS = 8
 class PeerExchange(C.Structure):
     _fields_ = [("nranks", C.c_uint32), ("rank", C.c_uint32), ("gather", C.c_void_p * MAX_PEERS),
                 ("flags", C.c_void_p * MAX_PEERS), ("step", C.c_void_p), ("done", C.c_void_p),
-                ("spin_limit", C.c_uint32)]
+                ("tickets", C.c_void_p), ("spin_limit", C.c_uint32)]
 
 
 class BgError(RuntimeError):
@@ -90,10 +90,9 @@ _SIGS = {
     "bg_attention_noalloc_limit": (SZ, []),
     "bg_peer_exchange_bytes": (SZ, [U32, U32, U32]),
     "bg_peer_exchange_flags_offset": (SZ, [U32, U32, U32]),
-    "bg_attention_partials_peer_workspace_size": (SZ, [C.POINTER(AttnParams), U32]),
-    "bg_attention_partials_peer": (C.c_int, [C.POINTER(AttnParams), U32, P, U32, C.POINTER(KVCacheDesc), P, P, F, U32,
-                                             U32, C.POINTER(PeerExchange), P, SZ, P]),
-    "bg_lse_merge_peer": (C.c_int, [C.POINTER(PeerExchange), U32, U32, P, P, U32, P]),
+    "bg_attention_peer_workspace_size": (SZ, [C.POINTER(AttnParams), U32]),
+    "bg_attention_peer": (C.c_int, [C.POINTER(AttnParams), U32, P, U32, C.POINTER(KVCacheDesc), F, U32, U32,
+                                    C.POINTER(PeerExchange), P, P, U32, P, SZ, P]),
     "bg_selftest_wait_expiry": (C.c_int, [U32, P]),
     "bg_attention_noalloc": (C.c_int, [C.POINTER(AttnParams), U32, P, U32, C.POINTER(KVCacheDesc), P, P, F, P, P,
                                        U32, P]),

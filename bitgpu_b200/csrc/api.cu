@@ -95,6 +95,8 @@ int run_attention(const bg_attn_params *p, uint32_t batch, const void *q, uint32
     return launch_prefill_tc(pa, st);
   }
   AttnArgs a;
+  a.px.nranks = 0;
+  a.fout = nullptr;
   a.q = q;
   a.q_f16 = q_dtype == BG_DT_F16;
   a.kv = make_view(kv, p->KV, row_offset);
@@ -135,10 +137,23 @@ int run_attention(const bg_attn_params *p, uint32_t batch, const void *q, uint32
     if (ws_bytes < part_bytes(a.nsplit, rows, p->D) || (!ws && rows)) return BG_ENOMEM;
     a.partials = static_cast<float *>(ws);
   }
+  if (peer && tc && !cosT) {
+    a.px = peer_args(peer, (uint32_t)rows);
+    a.fout = out;
+    a.out_f16 = out_dtype == BG_DT_F16;
+    a.gate = gate;
+  }
   int rc = tc ? launch_attn_tc(a, st) : BG_EUNSUPPORTED;
+  if (rc == BG_EUNSUPPORTED) a.px.nranks = 0;  // the CUDA-core kernel has no fused epilogue
   if (rc == BG_EUNSUPPORTED) rc = launch_attn_generic(a, st);
   if (rc || a.nsplit == 1) return rc;
-  if (peer) return launch_lse_push(a.partials, a.nsplit, (uint32_t)rows, p->D, peer, st);
+  if (peer) {
+    // the tensor-core kernel took the whole step (fused epilogue); the CUDA-core one left split
+    // partials: push them, then the merge kernel waits for the other ranks and writes out
+    if (a.px.nranks) return BG_OK;
+    rc = launch_lse_push(a.partials, a.nsplit, (uint32_t)rows, p->D, peer, st);
+    return rc ? rc : launch_lse_merge_peer(peer, (uint32_t)rows, p->D, gate, out, out_dtype == BG_DT_F16, st);
+  }
   if (partials_out) return launch_lse_merge(a.partials, a.nsplit, (uint32_t)rows, p->D, nullptr, partials_out, -1, st);
   return launch_lse_merge(a.partials, a.nsplit, (uint32_t)rows, p->D, gate, out, out_dtype == BG_DT_F16, st);
 }
@@ -257,6 +272,7 @@ int bg_device_status(bg_stream_t stream) {
   if (!e) e = poll_device_error_selftest();
   if (!e) e = poll_device_error_prefill_tf32();
   if (!e) e = poll_device_error_deltanet();
+  if (!e) e = poll_device_error_dnchunk();
   if (!e) e = poll_device_error_peer();
   return e ? (e < 0 ? e : BG_ELAUNCH) : BG_OK;
 }
@@ -324,42 +340,36 @@ size_t bg_peer_exchange_flags_offset(uint32_t nranks, uint32_t rows, uint32_t D)
 }
 
 size_t bg_peer_exchange_bytes(uint32_t nranks, uint32_t rows, uint32_t D) {
-  return bg_peer_exchange_flags_offset(nranks, rows, D) + ((size_t)nranks * sizeof(uint32_t) + 255) / 256 * 256;
+  return bg_peer_exchange_flags_offset(nranks, rows, D) + ((size_t)nranks * rows * sizeof(uint32_t) + 255) / 256 * 256;
 }
 
-size_t bg_attention_partials_peer_workspace_size(const bg_attn_params *p, uint32_t batch) {
+size_t bg_attention_peer_workspace_size(const bg_attn_params *p, uint32_t batch) {
   if (!p || !p->KV || !p->H) return 0;
   const size_t two = part_bytes(2, (uint64_t)batch * p->S * p->H, p->D);
   const size_t ws = attention_split_workspace_bytes(p, batch);
   return ws > two ? ws : two;
 }
 
-int bg_attention_partials_peer(const bg_attn_params *p, uint32_t batch, const void *q, uint32_t q_dtype,
-                               const bg_kv_cache *kv, const float *cosT, const float *sinT, float scale,
-                               uint32_t pos_lo, uint32_t pos_hi, const bg_peer_exchange *x, void *workspace,
-                               size_t workspace_bytes, bg_stream_t stream) {
+int bg_attention_peer(const bg_attn_params *p, uint32_t batch, const void *q, uint32_t q_dtype, const bg_kv_cache *kv,
+                      float scale, uint32_t pos_lo, uint32_t pos_hi, const bg_peer_exchange *x, const float *gate,
+                      void *out, uint32_t out_dtype, void *workspace, size_t workspace_bytes, bg_stream_t stream) {
   if (int rc = check_peer(x)) return rc;
-  if (!p || !kv || !q || q_dtype > BG_DT_F16) return BG_EINVAL;
+  if (!p || !kv || !q || !out || q_dtype > BG_DT_F16 || out_dtype > BG_DT_F16) return BG_EINVAL;
   if (p->H == 0 || p->KV == 0 || p->H % p->KV || !kv_mode_ok(kv->mode)) return BG_EINVAL;
   if (!d_ok(p->D)) return BG_EUNSUPPORTED;
   if (p->Ltot != p->posBase + p->S || pos_lo > pos_hi || pos_hi > p->Ltot) return BG_EINVAL;
   if (kv->window) return BG_EUNSUPPORTED;
   if (pos_hi - pos_lo > kv->seq_stride) return BG_EINVAL;
-  if ((cosT == nullptr) != (sinT == nullptr)) return BG_EINVAL;
+  if (!x->tickets) return BG_EINVAL;
   if (batch == 0 || p->S == 0) return BG_OK;
-  // the other ranks wait for this rank's rows every step, also when its slice attends nothing
-  if (pos_hi == pos_lo) return launch_lse_push(nullptr, 0, batch * p->S * p->H, p->D, x, (cudaStream_t)stream);
-  return run_attention(p, batch, q, q_dtype, kv, cosT, sinT, scale, pos_lo, pos_hi, pos_lo, nullptr, nullptr, nullptr,
-                       0, workspace, workspace_bytes, (cudaStream_t)stream, x);
-}
-
-int bg_lse_merge_peer(const bg_peer_exchange *x, uint32_t rows, uint32_t D, const float *gate, void *out,
-                      uint32_t out_dtype, bg_stream_t stream) {
-  int rc = check_peer(x);
-  if (rc) return rc;
-  if (!out || out_dtype > BG_DT_F16) return BG_EINVAL;
-  if (rows == 0) return BG_OK;
-  return launch_lse_merge_peer(x, rows, D, gate, out, out_dtype == BG_DT_F16, (cudaStream_t)stream);
+  const uint32_t rows = batch * p->S * p->H;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (pos_hi == pos_lo) {  // this slice attends nothing: push empty rows, then merge the others'
+    int rc = launch_lse_push(nullptr, 0, rows, p->D, x, st);
+    return rc ? rc : launch_lse_merge_peer(x, rows, p->D, gate, out, out_dtype == BG_DT_F16, st);
+  }
+  return run_attention(p, batch, q, q_dtype, kv, nullptr, nullptr, scale, pos_lo, pos_hi, pos_lo, nullptr, gate, out,
+                       out_dtype, workspace, workspace_bytes, st, x);
 }
 
 int bg_kv_append(const bg_kv_cache *kv, uint32_t which, uint32_t batch, const void *src, uint32_t src_dtype,

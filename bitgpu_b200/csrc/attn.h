@@ -1,6 +1,7 @@
 // Internal launch interface shared by the attention kernels and the C-ABI layer.
 #pragma once
 #include "common.cuh"
+#include "merge.cuh"
 
 namespace bg {
 
@@ -20,6 +21,11 @@ struct AttnArgs {
   void *out;
   int out_f16;
   const float *gate;
+  // peer-exchange step (tensor-core kernel, nsplit >= 2): the last CTA of each (sequence, kv head)
+  // group merges its splits, pushes the rows to every rank, waits for theirs and writes the final
+  // (gated) rows to fout -- px.nranks == 0: off
+  PeerArgs px;
+  void *fout;
 };
 
 // Number of KV splits for one attention call over L positions with the given cache mode and
@@ -53,6 +59,7 @@ int launch_lse_push(const float *partials, uint32_t nsplit, uint32_t rows, uint3
 int launch_lse_merge_peer(const bg_peer_exchange *x, uint32_t rows, uint32_t D, const float *gate, void *out,
                           int out_f16, cudaStream_t st);
 int poll_device_error_peer();
+PeerArgs peer_args(const bg_peer_exchange *x, uint32_t rows);
 int poll_device_error_attn_roll();
 
 }  // namespace bg

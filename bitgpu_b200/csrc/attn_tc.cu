@@ -52,7 +52,77 @@ struct TcParams {
   const float *Ksp, *Vsp;
   uint64_t seq_stride;
   uint32_t sinks, window, ring_head;
+  // peer-exchange step (px.nranks > 0): fused group epilogue, final rows to fout
+  PeerArgs px;
+  void *fout;
 };
+
+// Epilogue of the peer-exchange step, run by the four consumer warps (named barrier 1) of the CTA
+// that finished last among the gridDim.x splits of its (sequence, kv head) group:
+//   A  merge the group's split partials per row (log-sum-exp) and store each row into slot
+//      (step parity, this rank) of every rank's gather buffer over NVLink;
+//   B  count each row on every rank (system-scope release after a system fence);
+//   C  per row, wait (bounded) until every rank's counter reached this step, merge the nranks rows,
+//      apply the gate and write the output;
+//   D  free the group's ticket; the last group of this rank to finish advances the step counter.
+template <int D>
+__device__ __noinline__ void peer_group_epilogue(const TcParams &p, uint32_t b, uint32_t kvh, uint32_t nsplit,
+                                                 int tid) {
+  constexpr int DPL = D / 32;
+  const int warp = tid >> 5, lane = tid & 31;
+  const PeerArgs &x = p.px;
+  const uint32_t e = *x.step + 1, rows = x.rows;
+  auto grow_of = [&](uint32_t n) { return ((uint64_t)b * p.S + n / p.G) * p.H + kvh * p.G + n % p.G; };
+  for (uint32_t n = warp; n < p.M; n += 4) {
+    const uint64_t g = grow_of(n);
+    float acc[DPL], M, L;
+    merge_rows<DPL, true>(p.partials + g * (D + 2), (uint64_t)p.nrows_total * (D + 2), nsplit, lane, acc, M, L);
+    const uint64_t off = (((uint64_t)(e & 1) * x.nranks + x.rank) * rows + g) * (D + 2);
+    for (uint32_t r = 0; r < x.nranks; ++r) {
+      float *dst = x.gather[r] + off;
+#pragma unroll
+      for (int j = 0; j < DPL; ++j) dst[lane + 32 * j] = acc[j];
+      if (lane == 0) {
+        dst[D] = L > 0.f ? M : -INFINITY;
+        dst[D + 1] = L;
+      }
+    }
+  }
+  __threadfence_system();
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  for (uint32_t i = tid; i < p.M * x.nranks; i += 128)
+    atomicAdd_system(x.flags[i / p.M] + (uint64_t)x.rank * rows + grow_of(i % p.M), 1u);
+  for (uint32_t n = warp; n < p.M; n += 4) {
+    const uint64_t g = grow_of(n);
+    int ok = 1;
+    if (lane == 0) ok = peer_wait_row(x, (uint32_t)g, e, &g_device_error);
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    float acc[DPL], M = -INFINITY, L = 0.f;
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) acc[j] = 0.f;
+    if (ok)
+      merge_rows<DPL, true>(x.gather[x.rank] + ((uint64_t)(e & 1) * x.nranks * rows + g) * (D + 2),
+                            (uint64_t)rows * (D + 2), x.nranks, lane, acc, M, L);
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) {
+      const uint64_t i = g * D + lane + 32 * j;
+      float o = L > 0.f ? acc[j] / L : 0.f;
+      if (p.gate) o = o / (1.0f + expf(-p.gate[i]));
+      if (p.out_f16) static_cast<__half *>(p.fout)[i] = __float2half_rn(o);
+      else static_cast<float *>(p.fout)[i] = o;
+    }
+  }
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  if (tid == 0) {
+    x.tickets[blockIdx.y] = 0;
+    __threadfence();
+    if (atomicAdd(x.done, 1u) == gridDim.y - 1) {
+      *x.done = 0;
+      __threadfence();
+      atomicAdd(x.step, 1u);
+    }
+  }
+}
 
 template <int MODE, int D>
 struct Cfg {
@@ -640,6 +710,20 @@ __global__ void __launch_bounds__(160, (MODE == BG_KV_Q8 && NT == 1 && D == 128 
       dst[D + 1] = L;
     }
   }
+  if constexpr (!ROLL) {
+    if (p.px.nranks) {
+      // the group's last CTA (a ticket per (sequence, kv head)) finishes the whole step
+      __threadfence();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      volatile int *last = reinterpret_cast<volatile int *>(smem);  // ep is no longer read
+      if (tid == 0) *last = atomicAdd(p.px.tickets + blockIdx.y, 1u) == gridDim.x - 1;
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (*last) {
+        __threadfence();
+        peer_group_epilogue<D>(p, b, kvh, gridDim.x, tid);
+      }
+    }
+  }
 }
 
 template <int MODE, int D, int NT, bool ROLL>
@@ -691,6 +775,8 @@ int launch_cfg(const AttnArgs &a, cudaStream_t st) {
   p.sinks = a.kv.sinks;
   p.window = a.kv.window;
   p.ring_head = a.kv.ring_head;
+  p.px = a.px;
+  p.fout = a.fout;
   auto kern = attn_tc_kernel<MODE, D, NT, ROLL>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
     return BG_ELAUNCH;

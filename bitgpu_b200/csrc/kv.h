@@ -37,6 +37,7 @@ struct DeltaArgs {
 
 int launch_deltanet(const DeltaArgs &a, cudaStream_t st);
 int poll_device_error_deltanet();
+int poll_device_error_dnchunk();
 size_t deltanet_chunk_workspace(uint32_t S, uint32_t H);
 int launch_deltanet_chunked(const DeltaArgs &a, void *ws, size_t ws_bytes, cudaStream_t st);
 int launch_gbeta(const float *a, const float *b, const float *a_neg, const float *dt, uint32_t S, uint32_t H,

@@ -192,26 +192,25 @@ def attention_partials(q, cache, pos_base, pos_lo, pos_hi, scale=0.0, cos_t=None
     return part
 
 
-def attention_partials_peer(q, cache, pos_base, pos_lo, pos_hi, exchange, scale=0.0):
-    """Split-KV partials of this rank's slice stored straight into every rank's gather buffer
-    (``exchange``: a ``bitgpu_b200.splitkv.PeerExchange``); ``lse_merge_peer`` completes the step."""
+def attention_peer(q, cache, pos_base, pos_lo, pos_hi, exchange, scale=0.0, gate=None, out_dtype=torch.float32,
+                   out=None):
+    """One split-KV decode step over ranks that each hold positions ``[pos_lo, pos_hi)`` of the
+    stream in ``cache``: this rank's partials go straight into every rank's gather buffer
+    (``exchange``: a ``bitgpu_b200.splitkv.PeerExchange``) and the merged, gated rows come back in
+    ``out`` on every rank -- one kernel for f16 / q8 caches."""
+    _need(q, name="q")
     B, S, H, D = q.shape
     p = AttnParams(S, H, cache.KV, D, pos_base, pos_base + S)
-    nbytes = lib().bg_attention_partials_peer_workspace_size(C.byref(p), B)
+    if out is None:
+        out = torch.empty((B, S, H, D), dtype=out_dtype, device=q.device)
+    if gate is not None:
+        _need(gate, torch.float32, "gate")
+    nbytes = lib().bg_attention_peer_workspace_size(C.byref(p), B)
     ws = WORKSPACE.get(nbytes, q.device)
     d = cache.desc()
-    check("bg_attention_partials_peer", lib().bg_attention_partials_peer(
-        C.byref(p), B, _p(q), _DT[q.dtype], C.byref(d), None, None, float(scale), pos_lo, pos_hi,
-        C.byref(exchange.desc), _p(ws), ws.numel(), _stream()))
-
-
-def lse_merge_peer(exchange, out_shape, gate=None, out_dtype=torch.float32, out=None):
-    """Wait for every rank's rows of this step, merge them and apply the gate."""
-    if out is None:
-        out = torch.empty(out_shape, dtype=out_dtype, device="cuda")
-    rows = out.numel() // out.shape[-1]
-    check("bg_lse_merge_peer", lib().bg_lse_merge_peer(C.byref(exchange.desc), rows, out.shape[-1], _p(gate), _p(out),
-                                                        _DT[out.dtype], _stream()))
+    check("bg_attention_peer", lib().bg_attention_peer(C.byref(p), B, _p(q), _DT[q.dtype], C.byref(d), float(scale),
+                                                        pos_lo, pos_hi, C.byref(exchange.desc), _p(gate), _p(out),
+                                                        _DT[out.dtype], _p(ws), ws.numel(), _stream()))
     return out
 
 

@@ -13,11 +13,12 @@ over the ranks of one node.  Rank r holds the contiguous slice of cache position
 
 Step 2 has two forms:
 
-* ``exchange="peer"`` (default on GPUs): ``bg_attention_partials_peer`` stores the rows straight
-  into every rank's gather buffer over NVLink (plain peer stores into torch symmetric memory) and
-  raises per-source arrival counters; ``bg_lse_merge_peer`` waits for them with a bounded spin,
-  merges and gates.  Two kernels per step, no collective; the step counter lives on the device,
-  so a step can be captured in a CUDA graph.
+* ``exchange="peer"`` (default on GPUs): ``bg_attention_peer`` runs the whole step in one kernel
+  for f16 / q8 caches -- the last CTA of each (sequence, kv head) group merges its splits, stores
+  the rows straight into every rank's gather buffer over NVLink (plain peer stores into torch
+  symmetric memory), counts them on every rank, waits (bounded) for the other ranks' rows, merges
+  and gates.  No collective; the step counter lives on the device, so a step can be captured in a
+  CUDA graph.
 * ``exchange="nccl"``: ``bg_attention_partials``, one NCCL all-gather, ``bg_lse_merge`` (also the
   form the CPU tests run on ``gloo`` ranks).
 
@@ -39,9 +40,9 @@ class PeerFailure(RuntimeError):
 
 class PeerExchange:
     """One rank's side of the peer-memory exchange: a buffer every rank of ``group`` can address
-    (torch symmetric memory: gather slots ``[2][nranks][rows][D+2]`` f32, then ``nranks`` u32
-    arrival counters), this rank's step / merge counters, and the ``bg_peer_exchange`` descriptor
-    that carries every rank's addresses as seen from this GPU."""
+    (torch symmetric memory: gather slots ``[2][nranks][rows][D+2]`` f32, then ``[nranks][rows]`` u32
+    arrival counters), this rank's step / merge counters and per-group tickets, and the
+    ``bg_peer_exchange`` descriptor that carries every rank's addresses as seen from this GPU."""
 
     def __init__(self, rows, D, group=None, spin_limit=0):
         import torch.distributed._symmetric_memory as symm_mem
@@ -59,7 +60,7 @@ class PeerExchange:
         self.buf = symm_mem.empty(nbytes, dtype=torch.uint8, device=dev)
         self.buf.zero_()
         self.handle = symm_mem.rendezvous(self.buf, gname)
-        self.ctr = torch.zeros(2, dtype=torch.int32, device=dev)  # step, done
+        self.ctr = torch.zeros(2 + rows, dtype=torch.int32, device=dev)  # step, done, tickets (<= rows groups)
         ptrs = list(self.handle.buffer_ptrs)
         self.desc = Desc()
         self.desc.nranks, self.desc.rank = self.world, self.rank
@@ -68,6 +69,7 @@ class PeerExchange:
             self.desc.flags[r] = ptrs[r] + foff
         self.desc.step = self.ctr.data_ptr()
         self.desc.done = self.ctr.data_ptr() + 4
+        self.desc.tickets = self.ctr.data_ptr() + 8
         self.desc.spin_limit = spin_limit
         torch.cuda.synchronize()
         dist.barrier(group)  # every rank's buffer is zeroed before anyone pushes
@@ -133,8 +135,7 @@ class SplitKVDecoder:
             rows = B * S * H
             if self.px is None or (self.px.rows, self.px.D) != (rows, D):
                 self.px = PeerExchange(rows, D, self.group, self.spin_limit)
-            ops.attention_partials_peer(q, local_cache, pos_base, self.lo, hi, self.px, scale=scale)
-            return ops.lse_merge_peer(self.px, (B, S, H, D), gate=gate)
+            return ops.attention_peer(q, local_cache, pos_base, self.lo, hi, self.px, scale=scale, gate=gate)
         part = self.partials_fn(q, local_cache, pos_base, self.lo, hi, scale)
         if self.world == 1:
             gathered = part.unsqueeze(0)

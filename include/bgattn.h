@@ -132,33 +132,35 @@ int bg_lse_merge(const float *partials, uint32_t nsplit, uint32_t rows, uint32_t
                  const float *gate, void *out, uint32_t out_dtype, bg_stream_t stream);
 
 /* ---- split-KV exchange through peer memory (no reference counterpart) ----------------------
- * The partials / merge pair above with the all-gather replaced by NVLink peer stores: every rank
- * allocates one buffer of bg_peer_exchange_bytes(nranks, rows, D) bytes that all ranks can address
- * (e.g. torch symmetric memory, or CUDA IPC / VMM mappings), zeroed before the first step: the
- * gather slots [2][nranks][rows][D+2] f32 at offset 0, then nranks u32 arrival counters at
- * bg_peer_exchange_flags_offset(nranks, rows, D).  `step` and `done` are two zeroed u32 in this
- * rank's own device memory.  Per step, bg_attention_partials_peer stores this rank's rows into
- * every rank's slot and signals; bg_lse_merge_peer waits (bounded: spin_limit polls, 0 = default)
- * for every rank's rows of the same step, merges, gates and advances `step`.  Every rank must run
- * the same sequence of steps with the same shapes (rows = batch*S*H); steps may be captured in a
- * CUDA graph.  A wait that runs out shows as BG_ETIMEOUT in bg_device_status. */
+ * bg_attention_peer: one decode step of a stream whose cache positions are sharded over the ranks
+ * of one node, with the partials' exchange done by NVLink peer stores instead of a collective.
+ * Every rank allocates one buffer of bg_peer_exchange_bytes(nranks, rows, D) bytes that all ranks
+ * can address (e.g. torch symmetric memory, or CUDA IPC / VMM mappings), zeroed before the first
+ * step: gather slots [2][nranks][rows][D+2] f32 at offset 0, then per-row arrival counters
+ * [nranks][rows] u32 at bg_peer_exchange_flags_offset(nranks, rows, D); rows = batch*S*H.  `step`,
+ * `done` and `tickets` (batch*KV entries) are zeroed u32 in this rank's own device memory.
+ * Each rank passes its local slice [pos_lo, pos_hi) as in bg_attention_partials; out receives the
+ * merged, gated rows on every rank.  Tensor-core caches (f16, q8) run the whole step in one kernel
+ * (the last CTA of each (sequence, kv head) group merges its splits, stores the rows into every
+ * rank, waits -- bounded by spin_limit polls, 0 = default -- for the other ranks' rows and writes
+ * the output); other caches use a push kernel and a merge kernel.  Every rank must run the same
+ * sequence of steps with the same shapes; steps may be captured in a CUDA graph (the step number
+ * lives in `step`).  A wait that runs out shows as BG_ETIMEOUT in bg_device_status. */
 #define BG_MAX_PEERS 8
 typedef struct {
   uint32_t nranks, rank;
   float *gather[BG_MAX_PEERS];    /* rank r's buffer, as addressed from this GPU */
   uint32_t *flags[BG_MAX_PEERS];  /* rank r's arrival counters, as addressed from this GPU */
-  uint32_t *step, *done;          /* this rank's step counter and merge-completion counter */
+  uint32_t *step, *done, *tickets;
   uint32_t spin_limit;
 } bg_peer_exchange;
 size_t bg_peer_exchange_bytes(uint32_t nranks, uint32_t rows, uint32_t D);
 size_t bg_peer_exchange_flags_offset(uint32_t nranks, uint32_t rows, uint32_t D);
-size_t bg_attention_partials_peer_workspace_size(const bg_attn_params *p, uint32_t batch);
-int bg_attention_partials_peer(const bg_attn_params *p, uint32_t batch, const void *q, uint32_t q_dtype,
-                               const bg_kv_cache *kv, const float *cosT, const float *sinT, float scale,
-                               uint32_t pos_lo, uint32_t pos_hi, const bg_peer_exchange *x,
-                               void *workspace, size_t workspace_bytes, bg_stream_t stream);
-int bg_lse_merge_peer(const bg_peer_exchange *x, uint32_t rows, uint32_t D, const float *gate,
-                      void *out, uint32_t out_dtype, bg_stream_t stream);
+size_t bg_attention_peer_workspace_size(const bg_attn_params *p, uint32_t batch);
+int bg_attention_peer(const bg_attn_params *p, uint32_t batch, const void *q, uint32_t q_dtype,
+                      const bg_kv_cache *kv, float scale, uint32_t pos_lo, uint32_t pos_hi,
+                      const bg_peer_exchange *x, const float *gate, void *out, uint32_t out_dtype,
+                      void *workspace, size_t workspace_bytes, bg_stream_t stream);
 
 /* ---- KV cache writers ---------------------------------------------------------------------
  * bg_kv_append: appendKV(pass, src, which, li, rows, dstRow0) of src/engine.ts:1385-1393
