@@ -63,6 +63,9 @@ def parse():
                     help="configs measured as variants of the default decode run")
     ap.add_argument("--seq", type=int, default=8192, help="prefill tokens per sequence (config 3: 8192)")
     ap.add_argument("--prefill-batch", type=int, default=8, help="prefill sequences per GPU (config 3: 8)")
+    ap.add_argument("--prefill-cache", default="f16", choices=["f16", "q8", "f32"],
+                    help="--workload prefill: cache codec (q8: the engine's 8-bit cache; f32: 3xTF32 kernel)")
+    ap.add_argument("--prefill-q", default="f16", choices=["f16", "f32"], help="--workload prefill: query dtype")
 
     return ap.parse_args()
 
@@ -568,17 +571,20 @@ def run_ours(args):
     # ---------------- single-config workloads ----------------
     if args.workload == "prefill":
         clk = Clocks(local)
-        r = run_prefill(torch, ops, args, rank, barrier, max_over_ranks)
+        r = run_prefill(torch, ops, args, rank, barrier, max_over_ranks, mode=args.prefill_cache,
+                        q32=args.prefill_q == "f32", kv_write=args.prefill_cache == "f16" and args.prefill_q == "f16")
         per = r["flops"] / (r["ms"] * 1e-3) / 1e12
-        line = _base_line(args, ws, "prefill-attn TFLOP/s (config 3, Qwen3-4B shape, causal, f16)", per * ws,
+        line = _base_line(args, ws, "prefill-attn TFLOP/s (config 3, Qwen3-4B shape, causal)", per * ws,
                           "TFLOP/s", r["ms"], "f16",
                           {"workload": f"config 3: causal prefill, H32 KV8 D128, batch {args.prefill_batch}, "
-                                       f"seq {args.seq}, f16 Q/K/V, f32 accumulate, f16 out",
+                                       f"seq {args.seq}, {args.prefill_q} Q over a {args.prefill_cache} cache, "
+                                       f"f32 accumulate, f16 out",
                            "l2": "Q + K/V + out >> 126 MB L2"},
                           {"bound": "tensor", "achieved": round(per, 1), "peak": bf16_peak, "unit": "TFLOP/s",
                            "frac": round(per / bf16_peak, 4), "peak_kind": f"{peak_kind} cuBLAS bf16 burst",
                            "traffic": None}, args.steps, clk.stop())
-        line["kv_write"] = r["kv_write"]
+        if "kv_write" in r:
+            line["kv_write"] = r["kv_write"]
         return finish(line)
     if args.workload == "gated":
         clk = Clocks(local)
