@@ -51,6 +51,16 @@ KVView make_view(const bg_kv_cache *kv, uint32_t KV, uint32_t row_offset) {
   return v;
 }
 
+// BGATTN_PEER_FUSED=1 runs a peer-exchange step as one tensor-core kernel (the last CTA of each
+// group merges, pushes, waits and writes); default: the split kernel, a push kernel and a merge kernel
+bool peer_fused_enabled() {
+  static const bool v = [] {
+    const char *e = getenv("BGATTN_PEER_FUSED");
+    return e && e[0] == '1';
+  }();
+  return v;
+}
+
 // BGATTN_NSPLIT: split-count override for tuning sweeps (0 / unset = the cost model's choice).
 // bg_attention_workspace_size reserves for it, so an overridden call never under-allocates.
 uint32_t env_nsplit() {
@@ -137,7 +147,7 @@ int run_attention(const bg_attn_params *p, uint32_t batch, const void *q, uint32
     if (ws_bytes < part_bytes(a.nsplit, rows, p->D) || (!ws && rows)) return BG_ENOMEM;
     a.partials = static_cast<float *>(ws);
   }
-  if (peer && tc && !cosT) {
+  if (peer && tc && !cosT && peer_fused_enabled()) {
     a.px = peer_args(peer, (uint32_t)rows);
     a.fout = out;
     a.out_f16 = out_dtype == BG_DT_F16;

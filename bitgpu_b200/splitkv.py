@@ -13,11 +13,11 @@ over the ranks of one node.  Rank r holds the contiguous slice of cache position
 
 Step 2 has two forms:
 
-* ``exchange="peer"`` (default on GPUs): ``bg_attention_peer`` runs the whole step in one kernel
-  for f16 / q8 caches -- the last CTA of each (sequence, kv head) group merges its splits, stores
-  the rows straight into every rank's gather buffer over NVLink (plain peer stores into torch
-  symmetric memory), counts them on every rank, waits (bounded) for the other ranks' rows, merges
-  and gates.  No collective; the step counter lives on the device, so a step can be captured in a
+* ``exchange="peer"`` (default on GPUs): ``bg_attention_peer`` -- the split-KV kernel, then a
+  push kernel that merges this rank's splits and stores the rows straight into every rank's
+  gather buffer over NVLink (plain peer stores into torch symmetric memory) and counts them on
+  every rank, then a merge kernel that waits (bounded) for the other ranks' rows, merges and
+  gates.  No collective; the step counter lives on the device, so a step can be captured in a
   CUDA graph.
 * ``exchange="nccl"``: ``bg_attention_partials``, one NCCL all-gather, ``bg_lse_merge`` (also the
   form the CPU tests run on ``gloo`` ranks).

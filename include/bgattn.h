@@ -140,10 +140,10 @@ int bg_lse_merge(const float *partials, uint32_t nsplit, uint32_t rows, uint32_t
  * [nranks][rows] u32 at bg_peer_exchange_flags_offset(nranks, rows, D); rows = batch*S*H.  `step`,
  * `done` and `tickets` (batch*KV entries) are zeroed u32 in this rank's own device memory.
  * Each rank passes its local slice [pos_lo, pos_hi) as in bg_attention_partials; out receives the
- * merged, gated rows on every rank.  Tensor-core caches (f16, q8) run the whole step in one kernel
- * (the last CTA of each (sequence, kv head) group merges its splits, stores the rows into every
- * rank, waits -- bounded by spin_limit polls, 0 = default -- for the other ranks' rows and writes
- * the output); other caches use a push kernel and a merge kernel.  Every rank must run the same
+ * merged, gated rows on every rank.  After the split-KV kernel a push kernel merges this rank's
+ * splits and stores the rows into every rank; a merge kernel waits -- bounded by spin_limit polls,
+ * 0 = default -- for the other ranks' rows, merges and gates.  (BGATTN_PEER_FUSED=1 lets the
+ * tensor-core kernel do both in the last CTA of each (sequence, kv head) group instead.)  Every rank must run the same
  * sequence of steps with the same shapes; steps may be captured in a CUDA graph (the step number
  * lives in `step`).  A wait that runs out shows as BG_ETIMEOUT in bg_device_status. */
 #define BG_MAX_PEERS 8

@@ -3,8 +3,8 @@ partial rows go straight into every rank's gather buffer over NVLink and the mer
 arrival counters.  Run as two child processes, one per GPU (skipped with fewer than two GPUs).
 
 * parity: three consecutive steps (both parities of the double-buffered gather slots, the device
-  step counter) over f16 and q8 caches (one fused kernel per step) and an f32 cache (CUDA-core
-  kernel, push and merge kernels) equal single-GPU attention over the whole cache;
+  step counter) over f16, q8 and f32 caches equal single-GPU attention over the whole cache, with
+  the exchange as push + merge kernels and as the fused epilogue of the tensor-core kernel;
 * a CUDA-graph replay of the step gives the same result;
 * a rank that skips a step (stays alive, pushes nothing) makes the other rank's merge give up
   after its bounded wait and report BG_ETIMEOUT -- no hang, no fault."""
@@ -28,8 +28,9 @@ def _port():
     return p
 
 
-def _worker(rank, world, port, ret):
+def _worker(rank, world, port, ret, fused):
     import sys
+    os.environ["BGATTN_PEER_FUSED"] = fused   # read once, when the library is first used
     sys.path.insert(0, ROOT)
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -45,7 +46,7 @@ def _worker(rank, world, port, ret):
     Vf = torch.randn((1, L, KV, D), generator=g, device="cuda")
     errs = []
     decs = []
-    # f16 / q8: one fused tensor-core kernel per step; f32: CUDA-core kernel + push + merge kernels
+    # f16 / q8: tensor-core split kernel; f32: CUDA-core split kernel; then the exchange
     for mode in ("f16", "q8", "f32"):
         full = ops.KVCache(1, L, KV, D, mode=mode)
         full.append(0, Kf, 0)
@@ -97,11 +98,14 @@ def _worker(rank, world, port, ret):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_splitkv_peer_two_gpus():
+@pytest.mark.parametrize("fused", ["0", "1"])
+def test_splitkv_peer_two_gpus(fused):
+    """fused "0": split kernel, push kernel, merge kernel (default); "1": the tensor-core kernel
+    finishes the step in its last CTA per group."""
     ctx = mp.get_context("spawn")
     ret = ctx.Manager().dict()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, ret)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, ret, fused)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
