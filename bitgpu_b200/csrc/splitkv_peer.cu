@@ -12,9 +12,10 @@
 //   merge         for each row, wait (bounded spin, system-scope acquire) until every source's
 //                 counter for the row reaches the step number, merge the nranks rows, apply the
 //                 gate; the last CTA to finish advances this rank's step counter.
-// With the tensor-core decode kernel both happen in its epilogue (the last CTA of each (sequence,
-// kv head) group, found with a per-group ticket, merges, pushes, waits and writes the output), so
-// a step is one launch; this file holds the two-kernel form used behind the CUDA-core kernel.
+// These two kernels are the default step after either decode kernel.  The tensor-core decode
+// kernel can instead do both in its epilogue (the last CTA of each (sequence, kv head) group,
+// found with a per-group ticket, merges, pushes, waits and writes the output; opt-in with
+// BGATTN_PEER_FUSED=1), which makes a step one launch but measured no faster at 2 GPUs.
 //
 // The gather buffers are double-buffered by step parity: rank r can write step e+2 into a peer
 // only after its own merge of step e+1, which needed that peer's step-e+1 rows, which the peer
