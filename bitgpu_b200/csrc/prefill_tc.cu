@@ -37,10 +37,6 @@
 #include "tma.cuh"
 #include "umma.cuh"
 
-#ifndef BG_PREFILL_EX2_F16
-#define BG_PREFILL_EX2_F16 0
-#endif
-
 namespace bg {
 namespace {
 
@@ -450,19 +446,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t pk0[16], pk1[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-#if BG_PREFILL_EX2_F16
-          // two exponentials per MUFU op: the argument rounded to f16, the result is P's f16 itself
-          const uint32_t x01 = pack_half2(fmaf(__uint_as_float(r[c][2 * i]), sl2, mneg),
-                                          fmaf(__uint_as_float(r[c][2 * i + 1]), sl2, mneg));
-          const uint32_t x23 = pack_half2(fmaf(__uint_as_float(r[c + 1][2 * i]), sl2, mneg),
-                                          fmaf(__uint_as_float(r[c + 1][2 * i + 1]), sl2, mneg));
-          asm("ex2.approx.f16x2 %0, %1;" : "=r"(pk0[i]) : "r"(x01));
-          asm("ex2.approx.f16x2 %0, %1;" : "=r"(pk1[i]) : "r"(x23));
-          const float2 f01 = __half22float2(*reinterpret_cast<const __half2 *>(&pk0[i]));
-          const float2 f23 = __half22float2(*reinterpret_cast<const __half2 *>(&pk1[i]));
-          ls0 += f01.x + f01.y;
-          ls1 += f23.x + f23.y;
-#else
           const float p0 = ex2_approx(fmaf(__uint_as_float(r[c][2 * i]), sl2, mneg));
           const float p1 = ex2_approx(fmaf(__uint_as_float(r[c][2 * i + 1]), sl2, mneg));
           const float p2 = ex2_approx(fmaf(__uint_as_float(r[c + 1][2 * i]), sl2, mneg));
@@ -471,7 +454,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           ls1 += p2 + p3;
           pk0[i] = pack_half2(p0, p1);
           pk1[i] = pack_half2(p2, p3);
-#endif
         }
         tmem_st16(sbase + c * 16, pk0);
         tmem_st16(sbase + c * 16 + 16, pk1);
