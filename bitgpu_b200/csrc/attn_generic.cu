@@ -336,6 +336,84 @@ __global__ void __launch_bounds__(256) lse_merge_warp_kernel(const float *__rest
   }
 }
 
+// LSE merge for many splits: CTA (row, 64-column slice), its 8 warps take splits w, w + 8, ...;
+// each warp reduces (m, l) of every split (lane-strided), then loads its splits' 64 o values in
+// batches of 8 before any arithmetic, and the 8 partial sums meet in shared memory.  Launched as a
+// programmatic dependent of the decode kernel: its start-up overlaps that kernel's tail.
+constexpr int kWideCols = 64;
+
+__global__ void __launch_bounds__(256) lse_merge_wide_kernel(const float *__restrict__ part, uint32_t nsplit,
+                                                             uint32_t rows, uint32_t D, const float *__restrict__ gate,
+                                                             void *out, int out_f16) {
+  __shared__ float red[8][kWideCols];
+  __shared__ float lsum[8];
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t row = blockIdx.x, c0 = blockIdx.y * kWideCols;
+  const uint64_t stride = (uint64_t)rows * (D + 2);
+  const float *base = part + (uint64_t)row * (D + 2);
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  float M = -INFINITY;
+  for (uint32_t s = lane; s < nsplit; s += 32) {
+    const float l = __ldcg(base + s * stride + D + 1), m = __ldcg(base + s * stride + D);
+    if (l > 0.f) M = fmaxf(M, m);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  float a0 = 0.f, a1 = 0.f, L = 0.f;
+  for (uint32_t s0 = warp; s0 < nsplit; s0 += 64) {
+    float v0[8], v1[8], f[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t s = s0 + 8 * i;
+      const bool in = s < nsplit;
+      const float *src = base + (uint64_t)(in ? s : 0) * stride;
+      const float l = in ? __ldcg(src + D + 1) : 0.f, m = in ? __ldcg(src + D) : 0.f;
+      f[i] = l > 0.f ? expf(m - M) : 0.f;  // empty slots may hold any bits
+      L = fmaf(l > 0.f ? l : 0.f, f[i], L);
+      v0[i] = in ? __ldcg(src + c0 + lane) : 0.f;
+      v1[i] = in ? __ldcg(src + c0 + 32 + lane) : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (f[i] != 0.f) {
+        a0 = fmaf(v0[i], f[i], a0);
+        a1 = fmaf(v1[i], f[i], a1);
+      }
+    }
+  }
+  red[warp][lane] = a0;
+  red[warp][lane + 32] = a1;
+  if (lane == 0) lsum[warp] = L;
+  __syncthreads();
+  if (warp != 0) return;
+#pragma unroll
+  for (int w = 1; w < 8; ++w) {
+    a0 += red[w][lane];
+    a1 += red[w][lane + 32];
+  }
+  L = 0.f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) L += lsum[w];
+  if (out_f16 < 0) {
+    float *dst = static_cast<float *>(out) + (uint64_t)row * (D + 2);
+    dst[c0 + lane] = a0;
+    dst[c0 + 32 + lane] = a1;
+    if (c0 == 0 && lane == 0) {
+      dst[D] = L > 0.f ? M : -INFINITY;
+      dst[D + 1] = L;
+    }
+    return;
+  }
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const uint32_t d = c0 + lane + 32 * h;
+    float o = (h ? a1 : a0) / L;
+    if (gate) o = o / (1.0f + expf(-gate[(uint64_t)row * D + d]));
+    if (out_f16) static_cast<__half *>(out)[(uint64_t)row * D + d] = __float2half_rn(o);
+    else static_cast<float *>(out)[(uint64_t)row * D + d] = o;
+  }
+}
+
 template <int MODE, int D, bool ROLL>
 int launch_rb(const AttnArgs &a, cudaStream_t st) {
   const uint32_t rows = a.S * (a.H / a.KV);
@@ -497,6 +575,20 @@ int launch_lse_merge(const float *partials, uint32_t nsplit, uint32_t rows, uint
                      const float *gate, void *out, int out_f16, cudaStream_t st) {
   if (rows == 0) return BG_OK;
   if (D > 1024) return BG_EUNSUPPORTED;
+  if (nsplit > 16 && D % kWideCols == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(rows, D / kWideCols);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, lse_merge_wide_kernel, partials, nsplit, rows, D, gate, out, out_f16) == cudaSuccess
+               ? BG_OK
+               : BG_ELAUNCH;
+  }
   if (nsplit <= 8 * kMergeSpw && (D == 64 || D == 128 || D == 256)) {
     uint32_t wpr = 1;
     while (wpr * kMergeSpw < nsplit) wpr *= 2;

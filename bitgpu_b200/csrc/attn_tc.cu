@@ -35,6 +35,19 @@
 namespace bg {
 namespace {
 
+#ifdef BG_TRACE
+// Compile-time timing trace (-DBG_TRACE, never in the shipped build): per CTA of the last decode
+// launch, 8 u64 records -- [0] entry, [1] first tile ready, [2] last tile consumed, [5] partials
+// written (%globaltimer ns); [3] consumer warp 0's cycles waiting on full stages, [4] its cycles in
+// the tile loop, [6] SM id, [7] producer cycles waiting on empty stages.  Read with bg_trace_read.
+__device__ unsigned long long g_trace[8 * 8192];
+__device__ __forceinline__ unsigned long long gtime() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+#endif
+
 struct TcParams {
   const void *q;
   int q_f16;
@@ -136,8 +149,10 @@ struct Cfg {
   static constexpr int SCT = MODE == BG_KV_Q8 ? TP * NB * 4 : 0;
   static constexpr int STAGE = 2 * KVT + 2 * SCT;
   // q8 tiles are half the bytes of f16 ones but need more issue slots per byte: a smaller ring
-  // (72 KB) lets 3 CTAs share an SM; f16 keeps 96 KB rings at 2 CTAs per SM.
-  static constexpr int NST_RAW = (MODE == BG_KV_Q8 ? 73728 : 98304) / STAGE;
+  // (72 KB) lets 3 CTAs share an SM; f16 keeps 96 KB rings at 2 CTAs per SM.  D = 256 stages are
+  // so large that one CTA fills an SM; its ring takes ~200 KB (3 f16 / 5 q8 stages).
+  static constexpr int RING = D == 256 ? 204800 : (MODE == BG_KV_Q8 ? 73728 : 98304);
+  static constexpr int NST_RAW = RING / STAGE;
   static constexpr int NST = NST_RAW < 2 ? 2 : (NST_RAW > 6 ? 6 : NST_RAW);
   static constexpr int SMEM = NST * STAGE + 1024 /*align*/ + 2 * NST * 8 /*barriers*/ + 16 * NB * 4 /*q8 seeds*/;
 };
@@ -159,10 +174,23 @@ __global__ void __launch_bounds__(160, (MODE == BG_KV_Q8 && NT == 1 && D == 128 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t split = blockIdx.x;
   const uint32_t b = blockIdx.y / p.KV, kvh = blockIdx.y % p.KV;
+  // the merge kernel (a programmatic dependent) may be scheduled now: it waits for this grid's
+  // completion and memory flush in its own griddepcontrol.wait
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const uint32_t lo = p.pos_lo + split * p.chunk;
   uint32_t hi = min(p.pos_hi, lo + p.chunk);
   hi = min(hi, p.posBase + p.S);
   const int ntiles = hi > lo ? (int)((hi - lo + TP - 1) / TP) : 0;
+#ifdef BG_TRACE
+  unsigned long long *trc = g_trace + 8 * ((blockIdx.y * gridDim.x + blockIdx.x) & 8191);
+  if (tid == 0) {
+    uint32_t smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    trc[0] = gtime();
+    trc[6] = smid;
+  }
+  long long twait = 0, tloop0 = clock64();
+#endif
 
   if (tid == 0) {
     for (int s = 0; s < NST; ++s) {
@@ -243,7 +271,13 @@ __global__ void __launch_bounds__(160, (MODE == BG_KV_Q8 && NT == 1 && D == 128 
       bool ok = true;
       for (int t = 0; t < ntiles && ok; ++t) {
         const int s = t % NST;
+#ifdef BG_TRACE
+        const long long w0 = clock64();
+#endif
         if (t >= NST) ok = mbar_wait_warp(&empty[s], ((t / NST) - 1) & 1);
+#ifdef BG_TRACE
+        twait += clock64() - w0;
+#endif
         if (!ok) break;
         unsigned char *st = smem + s * C::STAGE;
         const int z = (int)(lo + t * TP - p.row_offset);
@@ -277,6 +311,9 @@ __global__ void __launch_bounds__(160, (MODE == BG_KV_Q8 && NT == 1 && D == 128 
       if (lane == 0)
         for (int t = max(0, ntiles - NST); t < ntiles; ++t) mbar_wait(&full[t % NST], (t / NST) & 1);
       asm volatile("cp.async.wait_all;" ::: "memory");
+#ifdef BG_TRACE
+      if (lane == 0) trc[7] = twait;
+#endif
     }
     return;
   }
@@ -362,12 +399,22 @@ __global__ void __launch_bounds__(160, (MODE == BG_KV_Q8 && NT == 1 && D == 128 
   const int trow = ((lane >> 4) << 3) + (lane & 7);         // .trans f16 V: matrices (pos, d) order
   const int tcol = (lane >> 3) & 1;
   bool ok = true;
+#ifdef BG_TRACE
+  tloop0 = clock64();
+#endif
   for (int t = 0; t < ntiles; ++t) {
     const int s = t % NST;
+#ifdef BG_TRACE
+    const long long w0 = clock64();
+#endif
     if (!mbar_wait_warp(&full[s], (t / NST) & 1)) {
       ok = false;
       break;
     }
+#ifdef BG_TRACE
+    twait += clock64() - w0;
+    if (t == 0 && tid == 0) trc[1] = gtime();
+#endif
     const uint32_t sb = smem_u32(smem + s * C::STAGE);
     const uint32_t kb = sb, vb = sb + C::KVT;
     const int row0 = warp * 16;
@@ -652,11 +699,24 @@ __global__ void __launch_bounds__(160, (MODE == BG_KV_Q8 && NT == 1 && D == 128 
     if (lane == 0) mbar_arrive(&empty[s]);
   }
 
+#ifdef BG_TRACE
+  if (tid == 0) {
+    trc[2] = gtime();
+    trc[3] = twait;
+    trc[4] = clock64() - tloop0;
+  }
+#endif
   // ---- merge the four warps' states; write split partials ----
-  constexpr int NN = NT * 8;
+  // (1) each warp's (m, l) per column; (2) every lane rescales its own o by exp2(m_warp - M) once
+  // per column and stores it, warp 0 keeps the merged (M, L) per column; (3) each output element
+  // is the plain sum of the four scaled values, four columns per thread.  Row stride D + 4 keeps
+  // the stores of (2) on distinct banks.
+  constexpr int NN = NT * 8, DP = D + 4;
   asm volatile("bar.sync 1, 128;" ::: "memory");  // all consumers done with the stages
-  float *ep = reinterpret_cast<float *>(smem);     // [NCW][NN][D+2]
-  float *mine = ep + warp * NN * (D + 2);
+  float *ep = reinterpret_cast<float *>(smem);     // [NCW][NN][DP] scaled o
+  float *mw = ep + C::NCW * NN * DP;               // [NCW][NN] m (log2 units)
+  float *lw = mw + C::NCW * NN;                    // [NCW][NN] l
+  float *mrow = lw + C::NCW * NN, *lsrow = mrow + NN;  // [NN] merged M, L
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
@@ -667,49 +727,77 @@ __global__ void __launch_bounds__(160, (MODE == BG_KV_Q8 && NT == 1 && D == 128 
       lt += __shfl_xor_sync(0xffffffffu, lt, 16);
       const int n = nt * 8 + 2 * (lane & 3) + j;
       if (lane < 4) {
-        mine[n * (D + 2) + D] = ok ? m[nt][j] : kNegBig;
-        mine[n * (D + 2) + D + 1] = ok ? lt : 0.f;
+        mw[warp * NN + n] = ok ? m[nt][j] : kNegBig;
+        lw[warp * NN + n] = ok ? lt : 0.f;  // timed out: an empty partial
       }
+    }
+  }
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int n = nt * 8 + 2 * (lane & 3) + j;
+      float M = kNegBig;
+#pragma unroll
+      for (int w = 0; w < C::NCW; ++w) M = fmaxf(M, mw[w * NN + n]);
+      const float f = ok ? exp2f(mw[warp * NN + n] - M) : 0.f;
+      if (warp == 0 && lane < 4) {
+        float L = 0.f;
+#pragma unroll
+        for (int w = 0; w < C::NCW; ++w) L = fmaf(lw[w * NN + n], exp2f(mw[w * NN + n] - M), L);
+        mrow[n] = M;
+        lsrow[n] = L;
+      }
+      float *mine = ep + (warp * NN + n) * DP;
 #pragma unroll
       for (int mt = 0; mt < KS; ++mt) {
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           const int d = MODE == BG_KV_F16 ? mt * 16 + (lane >> 2) + 8 * hh : mt * 16 + 2 * (lane >> 2) + hh;
-          mine[n * (D + 2) + d] = ok ? oacc[nt][mt][2 * hh + j] : 0.f;  // timed out: an empty partial
+          mine[d] = oacc[nt][mt][2 * hh + j] * f;
         }
       }
     }
   }
   asm volatile("bar.sync 1, 128;" ::: "memory");
-  for (int idx = tid; idx < (int)p.M * D; idx += C::NCW * 32) {
-    const int n = idx / D, d = idx % D;
-    float M = kNegBig;
-#pragma unroll
-    for (int w = 0; w < C::NCW; ++w) M = fmaxf(M, ep[(w * NN + n) * (D + 2) + D]);
-    float o = 0.f, L = 0.f;
+  for (int idx = tid; idx < (int)p.M * (D / 4); idx += C::NCW * 32) {
+    const int n = idx / (D / 4), d = (idx % (D / 4)) * 4;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int w = 0; w < C::NCW; ++w) {
-      const float *st = ep + (w * NN + n) * (D + 2);
-      const float f = exp2f(st[D] - M);
-      o = fmaf(st[d], f, o);
-      L = fmaf(st[D + 1], f, L);
+      const float4 x = *reinterpret_cast<const float4 *>(ep + (w * NN + n) * DP + d);
+      o.x += x.x; o.y += x.y; o.z += x.z; o.w += x.w;
     }
+    const float M = mrow[n], L = lsrow[n];
     const uint32_t qi = n / p.G, h = kvh * p.G + n % p.G;
     const uint64_t grow = ((uint64_t)b * p.S + qi) * p.H + h;
     if (p.out) {  // single split: final output
-      float v = L > 0.f ? o / L : 0.f;  // L == 0 only after a timed-out wait (BG_ETIMEOUT)
-      if (p.gate) v = v / (1.0f + expf(-p.gate[grow * D + d]));
-      if (p.out_f16) static_cast<__half *>(p.out)[grow * D + d] = __float2half_rn(v);
-      else static_cast<float *>(p.out)[grow * D + d] = v;
+      const float inv = L > 0.f ? 1.0f / L : 0.f;  // L == 0 only after a timed-out wait (BG_ETIMEOUT)
+      float v[4] = {o.x * inv, o.y * inv, o.z * inv, o.w * inv};
+      if (p.gate) {
+        const float4 g = *reinterpret_cast<const float4 *>(p.gate + grow * D + d);
+        const float gg[4] = {g.x, g.y, g.z, g.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = v[i] / (1.0f + expf(-gg[i]));
+      }
+      if (p.out_f16) {
+        const uint2 hv = make_uint2(pack_f16(v[0], v[1]), pack_f16(v[2], v[3]));
+        *reinterpret_cast<uint2 *>(static_cast<__half *>(p.out) + grow * D + d) = hv;
+      } else {
+        *reinterpret_cast<float4 *>(static_cast<float *>(p.out) + grow * D + d) = make_float4(v[0], v[1], v[2], v[3]);
+      }
       continue;
     }
     float *dst = p.partials + ((uint64_t)split * p.nrows_total + grow) * (D + 2);
-    dst[d] = o;
-    if (d == 0) {
-      dst[D] = L > 0.f ? M * kLn2 : -INFINITY;
-      dst[D + 1] = L;
-    }
+    *reinterpret_cast<float2 *>(dst + d) = make_float2(o.x, o.y);
+    *reinterpret_cast<float2 *>(dst + d + 2) = make_float2(o.z, o.w);
+    if (d == 0) *reinterpret_cast<float2 *>(dst + D) = make_float2(L > 0.f ? M * kLn2 : -INFINITY, L);
   }
+#ifdef BG_TRACE
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  if (tid == 0) trc[5] = gtime();
+#endif
   if constexpr (!ROLL) {
     if (p.px.nranks) {
       // the group's last CTA (a ticket per (sequence, kv head)) finishes the whole step
@@ -745,6 +833,8 @@ int launch_cfg(const AttnArgs &a, cudaStream_t st) {
     memset(&tk, 0, sizeof(tk));  // the cp.async producer of the ROLL kernels uses no tensor map
     tv = tks = tvs = tk;
   }
+  // the epilogue stores four columns at once: 16-byte aligned rows of out / gate, 8-byte partials
+  if (((uintptr_t)a.out | (uintptr_t)a.gate) & 15 || (uintptr_t)a.partials & 7) return BG_EUNSUPPORTED;
   TcParams p;
   p.q = a.q;
   p.q_f16 = a.q_f16;
@@ -860,3 +950,9 @@ int poll_device_error_attn_tc() {
 }
 
 }  // namespace bg
+
+#ifdef BG_TRACE
+extern "C" int bg_trace_read(unsigned long long *dst, size_t n) {
+  return cudaMemcpyFromSymbol(dst, bg::g_trace, n * sizeof(unsigned long long)) == cudaSuccess ? 0 : -1;
+}
+#endif
