@@ -202,13 +202,16 @@ __global__ void __launch_bounds__(256, 2) dn_chunk_prep(ChunkArgs p) {
     for (int r = 0; r < C; ++r) dst[r * DVc + col] = x[r];
   }
   if (tid < C) p.gcum[((uint64_t)h * p.nc + c) * C + tid] = gc[tid];
-  // decayed keys, transposed for the tensor-core scan: KT[dk][t] = Kn[t][dk] exp(gc_last - gc_t)
+  // decayed keys, transposed for the tensor-core scan: KT[dk][t] = Kn[t][dk] exp(gc_last - gc_t);
+  // the 64 decay factors once per value head (in beta's slot: beta is no longer read)
   if (p.KT) {
+    __syncthreads();  // every solve thread is done with beta
+    if (tid < C) beta[tid] = expf(gc[C - 1] - gc[tid]);
+    __syncthreads();
     float *kt = p.KT + ((uint64_t)h * p.nc + c) * DKc * C;
-    const float gl = gc[C - 1];
     for (int idx = tid; idx < DKc * C; idx += blockDim.x) {
       const int dk = idx / C, t = idx % C;
-      kt[idx] = kn[t * KP + dk] * expf(gl - gc[t]);
+      kt[idx] = kn[t * KP + dk] * beta[t];
     }
   }
   }
