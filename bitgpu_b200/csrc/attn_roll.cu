@@ -24,11 +24,12 @@
 //     (sequence, head group) cut by CTA boundaries leaves one partial per piece; the CTA holding
 //     the unit's first piece marks the unused partial slots empty, and the LSE merge kernel
 //     combines them.  When whole units fit per CTA the kernel writes the final rows itself.
-// Scores and outputs are computed transposed (S^T = K Q^T, O^T = V^T P^T, m16n8k16) exactly as in
-// the plain decode kernel, with Q split hi + lo.  K is dequantised and rotated in packed f16 (the
-// operand precision of the MMA; an f32 rotation rounded once was measured ~5% slower at half the
-// error, both far inside the 2e-3 gate).  Each consumer step takes two tiles when the piece has
-// them, so one max reduction covers 32 slots.
+// Scores and outputs are computed transposed (S^T = K Q^T, O^T = V^T P^T, m16n8k16) as in the
+// plain decode kernel, but with Q as one f16 operand: the rotated K is itself rounded to f16, so a
+// lo half of Q (the plain kernel's hi + lo split) would add MMAs without adding accuracy.  K is
+// dequantised and rotated in packed f16 (the operand precision of the MMA; an f32 rotation rounded
+// once was measured ~5% slower at half the error, both far inside the 2e-3 gate).  Each consumer
+// step takes two tiles when the piece has them, so one max reduction covers 32 slots.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <string.h>
@@ -267,7 +268,7 @@ __global__ void __launch_bounds__(RCfg<MODE, HPC>::THREADS, 1)
     const uint32_t b = pc.unit / p.units_per_seq, kvh = (pc.unit % p.units_per_seq) * HPC + warp;
 
     // Q^T fragments of this head's group rows (see the plain decode kernel for the k-slot order)
-    uint32_t qh[KS][2], ql[KS][2];
+    uint32_t qh[KS][2];
     uint32_t lim[2];
     {
       const uint32_t r = lane >> 2;
@@ -293,7 +294,6 @@ __global__ void __launch_bounds__(RCfg<MODE, HPC>::THREADS, 1)
           }
           const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
           qh[ks][half] = pack_f16(__half2float(h0), __half2float(h1));
-          ql[ks][half] = pack_f16(x0 - __half2float(h0), x1 - __half2float(h1));
         }
       }
 #pragma unroll
@@ -370,8 +370,6 @@ __global__ void __launch_bounds__(RCfg<MODE, HPC>::THREADS, 1)
         float (&ac)[4] = acc4[ks];
         mma16816(ac, al, qh[ks][0], qh[ks][1]);
         mma16816(ac, ah, qh[ks + KS / 2][0], qh[ks + KS / 2][1]);
-        mma16816(ac, al, ql[ks][0], ql[ks][1]);
-        mma16816(ac, ah, ql[ks + KS / 2][0], ql[ks + KS / 2][1]);
       };
       if constexpr (MODE == BG_KV_F16) {
 #pragma unroll
