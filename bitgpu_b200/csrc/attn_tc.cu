@@ -174,9 +174,9 @@ __global__ void __launch_bounds__(160, (MODE == BG_KV_Q8 && NT == 1 && D == 128 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t split = blockIdx.x;
   const uint32_t b = blockIdx.y / p.KV, kvh = blockIdx.y % p.KV;
-  // the merge kernel (a programmatic dependent) may be scheduled now: it waits for this grid's
-  // completion and memory flush in its own griddepcontrol.wait
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // No griddepcontrol.launch_dependents: the merge / push kernels are programmatic dependents, but
+  // scheduled at this kernel's entry their CTAs sat on the SMs beside the decode and cost ~6 us per
+  // 2-GPU config-5b step; with the implicit trigger at exit only their launch overlaps.
   const uint32_t lo = p.pos_lo + split * p.chunk;
   uint32_t hi = min(p.pos_hi, lo + p.chunk);
   hi = min(hi, p.posBase + p.S);

@@ -29,31 +29,77 @@
 namespace bg {
 namespace {
 
-// Rows [8 block, 8 block + 8), one warp per row: merge `nsplit` local partials, store the result
-// row into slot (parity, rank) of every rank's gather buffer, then count the row on every rank.
+// One CTA per row: its 8 warps merge the `nsplit` local partials (warp w: splits w, w + 8, ...,
+// loaded in batches of 8 before any arithmetic), the partial sums meet in shared memory, and warp 0
+// stores the row into slot (parity, rank) of every rank's gather buffer, then counts it on every
+// rank.  Launched as a programmatic dependent of the decode kernel (griddepcontrol.wait before the
+// first read of the partials).
 template <int DPL>
 __global__ void __launch_bounds__(256) lse_push_kernel(const float *__restrict__ part, uint32_t nsplit, PeerArgs x) {
   constexpr uint32_t D = DPL * 32;
+  __shared__ float red[8][D];
+  __shared__ float lsum[8];
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const uint32_t rows = x.rows, row = blockIdx.x * 8 + warp;
+  const uint32_t rows = x.rows, row = blockIdx.x;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const uint32_t e = *x.step + 1;
-  if (row < rows) {
-    float acc[DPL], M, L;
-    merge_rows<DPL, false>(part + (uint64_t)row * (D + 2), (uint64_t)rows * (D + 2), nsplit, lane, acc, M, L);
-    const uint64_t off = (((uint64_t)(e & 1) * x.nranks + x.rank) * rows + row) * (D + 2);
-    for (uint32_t r = 0; r < x.nranks; ++r) {
-      float *dst = x.gather[r] + off;
-#pragma unroll
-      for (int j = 0; j < DPL; ++j) dst[lane + 32 * j] = acc[j];
-      if (lane == 0) {
-        dst[D] = L > 0.f ? M : -INFINITY;
-        dst[D + 1] = L;
-      }
-    }
-    __threadfence_system();  // the row, in every rank, before its counters
-    __syncwarp();
-    if (lane < x.nranks) atomicAdd_system(x.flags[lane] + (uint64_t)x.rank * rows + row, 1u);
+  const uint64_t stride = (uint64_t)rows * (D + 2);
+  const float *base = part + (uint64_t)row * (D + 2);
+  float M = -INFINITY;
+  for (uint32_t s = lane; s < nsplit; s += 32) {
+    const float l = __ldcg(base + s * stride + D + 1), m = __ldcg(base + s * stride + D);
+    if (l > 0.f) M = fmaxf(M, m);
   }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  float acc[DPL], L = 0.f;
+#pragma unroll
+  for (int j = 0; j < DPL; ++j) acc[j] = 0.f;
+  for (uint32_t s0 = warp; s0 < nsplit; s0 += 64) {
+    float v[8][DPL], f[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t sp = s0 + 8 * i;
+      const bool in = sp < nsplit;
+      const float *src = base + (uint64_t)(in ? sp : 0) * stride;
+      const float l = in ? __ldcg(src + D + 1) : 0.f, m = in ? __ldcg(src + D) : 0.f;
+      f[i] = l > 0.f ? expf(m - M) : 0.f;  // empty slots may hold any bits
+      L = fmaf(l > 0.f ? l : 0.f, f[i], L);
+#pragma unroll
+      for (int j = 0; j < DPL; ++j) v[i][j] = in ? __ldcg(src + lane + 32 * j) : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (f[i] != 0.f)
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) acc[j] = fmaf(v[i][j], f[i], acc[j]);
+  }
+#pragma unroll
+  for (int j = 0; j < DPL; ++j) red[warp][lane + 32 * j] = acc[j];
+  if (lane == 0) lsum[warp] = L;
+  __syncthreads();
+  if (warp != 0) return;
+#pragma unroll
+  for (int w = 1; w < 8; ++w)
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) acc[j] += red[w][lane + 32 * j];
+  L = 0.f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) L += lsum[w];
+  const uint64_t off = (((uint64_t)(e & 1) * x.nranks + x.rank) * rows + row) * (D + 2);
+  for (uint32_t r = 0; r < x.nranks; ++r) {
+    float *dst = x.gather[r] + off;
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) dst[lane + 32 * j] = acc[j];
+    if (lane == 0) {
+      dst[D] = L > 0.f ? M : -INFINITY;
+      dst[D + 1] = L;
+    }
+  }
+  __threadfence_system();  // the row, in every rank, before its counters
+  __syncwarp();
+  if (lane < x.nranks) atomicAdd_system(x.flags[lane] + (uint64_t)x.rank * rows + row, 1u);
 }
 
 // One warp per row: wait for every rank's row of this step, merge, gate, write; the last CTA to
@@ -64,6 +110,8 @@ __global__ void __launch_bounds__(256) lse_merge_peer_kernel(PeerArgs x, const f
   constexpr uint32_t D = DPL * 32;
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t rows = x.rows, row = blockIdx.x * 8 + warp;
+  // a programmatic dependent of the push kernel: nothing is read before that grid completed
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const uint32_t e = *x.step + 1;
   if (row < rows) {
     int ok = 1;
@@ -95,6 +143,19 @@ __global__ void __launch_bounds__(256) lse_merge_peer_kernel(PeerArgs x, const f
   }
 }
 
+// 256-thread launch configuration with programmatic stream serialization (the kernel may be
+// scheduled while the previous one in the stream finishes; it waits in griddepcontrol.wait)
+void pdl_config(cudaLaunchConfig_t &cfg, cudaLaunchAttribute (&attr)[1], dim3 grid, cudaStream_t st) {
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+}
+
 }  // namespace
 
 PeerArgs peer_args(const bg_peer_exchange *x, uint32_t rows) {
@@ -116,23 +177,31 @@ PeerArgs peer_args(const bg_peer_exchange *x, uint32_t rows) {
 int launch_lse_push(const float *partials, uint32_t nsplit, uint32_t rows, uint32_t D, const bg_peer_exchange *x,
                     cudaStream_t st) {
   const PeerArgs a = peer_args(x, rows);
-  const uint32_t blocks = (rows + 7) / 8;
-  if (D == 64) lse_push_kernel<2><<<blocks, 256, 0, st>>>(partials, nsplit, a);
-  else if (D == 128) lse_push_kernel<4><<<blocks, 256, 0, st>>>(partials, nsplit, a);
-  else if (D == 256) lse_push_kernel<8><<<blocks, 256, 0, st>>>(partials, nsplit, a);
+  if (rows == 0) return BG_OK;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  pdl_config(cfg, attr, dim3(rows), st);
+  cudaError_t err;
+  if (D == 64) err = cudaLaunchKernelEx(&cfg, lse_push_kernel<2>, partials, nsplit, a);
+  else if (D == 128) err = cudaLaunchKernelEx(&cfg, lse_push_kernel<4>, partials, nsplit, a);
+  else if (D == 256) err = cudaLaunchKernelEx(&cfg, lse_push_kernel<8>, partials, nsplit, a);
   else return BG_EUNSUPPORTED;
-  return cudaGetLastError() == cudaSuccess ? BG_OK : BG_ELAUNCH;
+  return err == cudaSuccess ? BG_OK : BG_ELAUNCH;
 }
 
 int launch_lse_merge_peer(const bg_peer_exchange *x, uint32_t rows, uint32_t D, const float *gate, void *out,
                           int out_f16, cudaStream_t st) {
   const PeerArgs a = peer_args(x, rows);
   const uint32_t blocks = (rows + 7) / 8;
-  if (D == 64) lse_merge_peer_kernel<2><<<blocks, 256, 0, st>>>(a, gate, out, out_f16);
-  else if (D == 128) lse_merge_peer_kernel<4><<<blocks, 256, 0, st>>>(a, gate, out, out_f16);
-  else if (D == 256) lse_merge_peer_kernel<8><<<blocks, 256, 0, st>>>(a, gate, out, out_f16);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  pdl_config(cfg, attr, dim3(blocks), st);
+  cudaError_t err;
+  if (D == 64) err = cudaLaunchKernelEx(&cfg, lse_merge_peer_kernel<2>, a, gate, out, out_f16);
+  else if (D == 128) err = cudaLaunchKernelEx(&cfg, lse_merge_peer_kernel<4>, a, gate, out, out_f16);
+  else if (D == 256) err = cudaLaunchKernelEx(&cfg, lse_merge_peer_kernel<8>, a, gate, out, out_f16);
   else return BG_EUNSUPPORTED;
-  return cudaGetLastError() == cudaSuccess ? BG_OK : BG_ELAUNCH;
+  return err == cudaSuccess ? BG_OK : BG_ELAUNCH;
 }
 
 int poll_device_error_peer() {
