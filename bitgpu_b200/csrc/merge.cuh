@@ -39,6 +39,31 @@ __device__ __forceinline__ bool peer_wait_row(const PeerArgs &x, uint32_t row, u
   return true;
 }
 
+// Whole-warp form: lane r < nranks polls rank r's counter for `row` with relaxed system-scope loads,
+// all ranks in parallel, and one acquire fence follows once every counter reached `target`.
+// Returns the same value on every lane; false (BG_ETIMEOUT recorded) when a lane's limit ran out.
+__device__ __forceinline__ bool peer_wait_row_warp(const PeerArgs &x, uint32_t row, uint32_t target, int *err,
+                                                   uint32_t lane) {
+  bool ok = true;
+  if (lane < x.nranks) {
+    const uint32_t *f = x.flags[x.rank] + (uint64_t)lane * x.rows + row;
+    uint32_t it = 0, v;
+    for (;;) {
+      asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+      if ((int32_t)(v - target) >= 0) break;  // counters grow by one per step (wrap-safe)
+      if (++it > x.spin_limit) {
+        atomicExch(err, BG_ETIMEOUT);
+        ok = false;
+        break;
+      }
+      __nanosleep(32);
+    }
+  }
+  ok = __all_sync(0xffffffffu, ok);
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+  return ok;
+}
+
 // Weighted sum over `n` rows of stride `stride` (one warp, lane owns DPL columns): returns the
 // unnormalised o, the merged max M and sum L.  Each pass over 32 sources first loads every source's
 // (m, l) lane-parallel and then its o values in batches of 8 before any arithmetic, so a warp waits

@@ -9,8 +9,9 @@
 //                 each finished row is stored straight into every rank's gather buffer over NVLink
 //                 (plain peer stores; no TMA, no multicast); then the row's arrival counter on
 //                 every rank is incremented (system-scope release).
-//   merge         for each row, wait (bounded spin, system-scope acquire) until every source's
-//                 counter for the row reaches the step number, merge the nranks rows, apply the
+//   merge         for each row, wait (bounded spin: lane r polls rank r's counter with relaxed
+//                 system-scope loads, then one acquire fence) until every source's counter for
+//                 the row reaches the step number, merge the nranks rows, apply the
 //                 gate; the last CTA to finish advances this rank's step counter.
 // These two kernels are the default step after either decode kernel.  The tensor-core decode
 // kernel can instead do both in its epilogue (the last CTA of each (sequence, kv head) group,
@@ -29,8 +30,21 @@
 namespace bg {
 namespace {
 
-// One CTA per row: its 8 warps merge the `nsplit` local partials (warp w: splits w, w + 8, ...,
-// loaded in batches of 8 before any arithmetic), the partial sums meet in shared memory, and warp 0
+#ifdef BG_TRACE
+// Compile-time timing trace (-DBG_TRACE, never in the shipped build), %globaltimer ns of the last
+// step: push CTA r -> [r][0] entry (after its wait), [1] local merge done, [2] counters raised;
+// merge CTA c -> [256 + c][0] entry, [1] rows arrived, [2] done.  Read with bg_ptrace_read.
+__device__ unsigned long long g_ptrace[512][4];
+__device__ __forceinline__ unsigned long long ptime() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+#endif
+
+// One CTA per row: its 8 warps merge the `nsplit` local partials in one pass (warp w: splits w,
+// w + 8, ..., (m, l, o) loaded in batches of 8 before any arithmetic, a running max per warp), the
+// warp states meet in shared memory rescaled to the common max, and warp 0
 // stores the row into slot (parity, rank) of every rank's gather buffer, then counts it on every
 // rank.  Launched as a programmatic dependent of the decode kernel (griddepcontrol.wait before the
 // first read of the partials).
@@ -43,50 +57,75 @@ __global__ void __launch_bounds__(256) lse_push_kernel(const float *__restrict__
   const uint32_t rows = x.rows, row = blockIdx.x;
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+#ifdef BG_TRACE
+  if (threadIdx.x == 0 && row < 256) g_ptrace[row][0] = ptime();
+#endif
   const uint32_t e = *x.step + 1;
   const uint64_t stride = (uint64_t)rows * (D + 2);
   const float *base = part + (uint64_t)row * (D + 2);
-  float M = -INFINITY;
-  for (uint32_t s = lane; s < nsplit; s += 32) {
-    const float l = __ldcg(base + s * stride + D + 1), m = __ldcg(base + s * stride + D);
-    if (l > 0.f) M = fmaxf(M, m);
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-  float acc[DPL], L = 0.f;
+  // one pass: each warp loads (m, l, o) of its splits in batches of 8 and keeps a running
+  // (max, sum, o) of its own; the 8 warp states are rescaled to the common max in shared memory
+  float acc[DPL], L = 0.f, Mw = -INFINITY;
 #pragma unroll
   for (int j = 0; j < DPL; ++j) acc[j] = 0.f;
   for (uint32_t s0 = warp; s0 < nsplit; s0 += 64) {
-    float v[8][DPL], f[8];
+    float v[8][DPL], mv[8], lv[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const uint32_t sp = s0 + 8 * i;
       const bool in = sp < nsplit;
       const float *src = base + (uint64_t)(in ? sp : 0) * stride;
-      const float l = in ? __ldcg(src + D + 1) : 0.f, m = in ? __ldcg(src + D) : 0.f;
-      f[i] = l > 0.f ? expf(m - M) : 0.f;  // empty slots may hold any bits
-      L = fmaf(l > 0.f ? l : 0.f, f[i], L);
+      lv[i] = in ? __ldcg(src + D + 1) : 0.f;
+      mv[i] = in ? __ldcg(src + D) : 0.f;
 #pragma unroll
       for (int j = 0; j < DPL; ++j) v[i][j] = in ? __ldcg(src + lane + 32 * j) : 0.f;
     }
+    float Mb = Mw;
 #pragma unroll
     for (int i = 0; i < 8; ++i)
-      if (f[i] != 0.f)
+      if (lv[i] > 0.f) Mb = fmaxf(Mb, mv[i]);  // empty slots may hold any bits
+    if (Mb != Mw) {
+      const float c = Mw == -INFINITY ? 0.f : expf(Mw - Mb);
+      L *= c;
 #pragma unroll
-        for (int j = 0; j < DPL; ++j) acc[j] = fmaf(v[i][j], f[i], acc[j]);
+      for (int j = 0; j < DPL; ++j) acc[j] *= c;
+      Mw = Mb;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (lv[i] > 0.f) {
+        const float f = expf(mv[i] - Mw);
+        L = fmaf(lv[i], f, L);
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) acc[j] = fmaf(v[i][j], f, acc[j]);
+      }
+    }
   }
+  __shared__ float mws[8];
 #pragma unroll
   for (int j = 0; j < DPL; ++j) red[warp][lane + 32 * j] = acc[j];
-  if (lane == 0) lsum[warp] = L;
+  if (lane == 0) {
+    lsum[warp] = L;
+    mws[warp] = Mw;
+  }
   __syncthreads();
   if (warp != 0) return;
+  float M = -INFINITY;
 #pragma unroll
-  for (int w = 1; w < 8; ++w)
-#pragma unroll
-    for (int j = 0; j < DPL; ++j) acc[j] += red[w][lane + 32 * j];
+  for (int w = 0; w < 8; ++w) M = fmaxf(M, mws[w]);
   L = 0.f;
 #pragma unroll
-  for (int w = 0; w < 8; ++w) L += lsum[w];
+  for (int j = 0; j < DPL; ++j) acc[j] = 0.f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    const float f = mws[w] == -INFINITY ? 0.f : expf(mws[w] - M);
+    L = fmaf(lsum[w], f, L);
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) acc[j] = fmaf(red[w][lane + 32 * j], f, acc[j]);
+  }
+#ifdef BG_TRACE
+  if (lane == 0 && row < 256) g_ptrace[row][1] = ptime();
+#endif
   const uint64_t off = (((uint64_t)(e & 1) * x.nranks + x.rank) * rows + row) * (D + 2);
   for (uint32_t r = 0; r < x.nranks; ++r) {
     float *dst = x.gather[r] + off;
@@ -100,6 +139,9 @@ __global__ void __launch_bounds__(256) lse_push_kernel(const float *__restrict__
   __threadfence_system();  // the row, in every rank, before its counters
   __syncwarp();
   if (lane < x.nranks) atomicAdd_system(x.flags[lane] + (uint64_t)x.rank * rows + row, 1u);
+#ifdef BG_TRACE
+  if (lane == 0 && row < 256) g_ptrace[row][2] = ptime();
+#endif
 }
 
 // One warp per row: wait for every rank's row of this step, merge, gate, write; the last CTA to
@@ -112,11 +154,15 @@ __global__ void __launch_bounds__(256) lse_merge_peer_kernel(PeerArgs x, const f
   const uint32_t rows = x.rows, row = blockIdx.x * 8 + warp;
   // a programmatic dependent of the push kernel: nothing is read before that grid completed
   asm volatile("griddepcontrol.wait;" ::: "memory");
+#ifdef BG_TRACE
+  if (threadIdx.x == 0 && blockIdx.x < 256) g_ptrace[256 + blockIdx.x][0] = ptime();
+#endif
   const uint32_t e = *x.step + 1;
   if (row < rows) {
-    int ok = 1;
-    if (lane == 0) ok = peer_wait_row(x, row, e, &g_device_error);
-    ok = __shfl_sync(0xffffffffu, ok, 0);
+    const bool ok = peer_wait_row_warp(x, row, e, &g_device_error, lane);
+#ifdef BG_TRACE
+    if (lane == 0 && warp == 0 && blockIdx.x < 256) g_ptrace[256 + blockIdx.x][1] = ptime();
+#endif
     float acc[DPL], M = -INFINITY, L = 0.f;
 #pragma unroll
     for (int j = 0; j < DPL; ++j) acc[j] = 0.f;
@@ -133,6 +179,9 @@ __global__ void __launch_bounds__(256) lse_merge_peer_kernel(PeerArgs x, const f
     }
   }
   __syncthreads();
+#ifdef BG_TRACE
+  if (threadIdx.x == 0 && blockIdx.x < 256) g_ptrace[256 + blockIdx.x][2] = ptime();
+#endif
   if (threadIdx.x == 0) {
     __threadfence();
     if (atomicAdd(x.done, 1u) == gridDim.x - 1) {
@@ -212,3 +261,9 @@ int poll_device_error_peer() {
 }
 
 }  // namespace bg
+
+#ifdef BG_TRACE
+extern "C" int bg_ptrace_read(unsigned long long *dst, size_t n) {
+  return cudaMemcpyFromSymbol(dst, bg::g_ptrace, n * sizeof(unsigned long long)) == cudaSuccess ? 0 : -1;
+}
+#endif
