@@ -255,3 +255,30 @@ def test_roll_head_groups(ops, mode, H, KV, S):
         assert ok, (mode, H, KV, S, b, mad, cs)
     assert lib().bg_device_status(None) == 0
 
+
+
+@pytest.mark.parametrize("D", [64, 128, 256])
+@pytest.mark.parametrize("nsplit", [17, 40, 130])
+def test_lse_merge_many_splits(ops, D, nsplit):
+    """bg_lse_merge beyond 16 splits (the column-sliced merge kernel) against a numpy log-sum-exp
+    merge, gated output; empty splits (l = 0 with arbitrary m / o bits) are skipped."""
+    rng = np.random.default_rng(nsplit + D)
+    rows = 24
+    o = rng.standard_normal((nsplit, rows, D)).astype(np.float32)
+    m = (3.0 * rng.standard_normal((nsplit, rows))).astype(np.float32)
+    l = rng.uniform(0.5, 4.0, (nsplit, rows)).astype(np.float32)
+    empty = rng.random((nsplit, rows)) < 0.2
+    empty[0] = False
+    l[empty] = 0.0
+    o[empty] = np.nan
+    m[empty] = np.nan
+    part = np.concatenate([o, m[..., None], l[..., None]], axis=-1)
+    gate = rng.standard_normal((1, 1, rows, D)).astype(np.float32)
+    w = np.where(empty, 0.0, np.exp(np.where(empty, 0.0, m) - np.nanmax(np.where(empty, -np.inf, m), axis=0)))
+    num = np.einsum("sr,srd->rd", w, np.where(empty[..., None], 0.0, o))
+    den = (w * l).sum(0)
+    exp = (num / den[:, None]) / (1.0 + np.exp(-gate[0, 0]))
+    out = ops.lse_merge(torch.from_numpy(part).cuda(), (1, 1, rows, D), gate=torch.from_numpy(gate).cuda())
+    got = out.cpu().numpy()[0, 0]
+    assert np.isfinite(got).all()
+    assert np.abs(got - exp).max() < 1e-5 * max(1.0, np.abs(exp).max())
