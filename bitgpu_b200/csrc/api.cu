@@ -161,8 +161,7 @@ int run_attention(const bg_attn_params *p, uint32_t batch, const void *q, uint32
     // the tensor-core kernel took the whole step (fused epilogue); the CUDA-core one left split
     // partials: push them, then the merge kernel waits for the other ranks and writes out
     if (a.px.nranks) return BG_OK;
-    rc = launch_lse_push(a.partials, a.nsplit, (uint32_t)rows, p->D, peer, st);
-    return rc ? rc : launch_lse_merge_peer(peer, (uint32_t)rows, p->D, gate, out, out_dtype == BG_DT_F16, st);
+    return launch_lse_exchange(a.partials, a.nsplit, (uint32_t)rows, p->D, peer, gate, out, out_dtype == BG_DT_F16, st);
   }
   if (partials_out) return launch_lse_merge(a.partials, a.nsplit, (uint32_t)rows, p->D, nullptr, partials_out, -1, st);
   return launch_lse_merge(a.partials, a.nsplit, (uint32_t)rows, p->D, gate, out, out_dtype == BG_DT_F16, st);
@@ -375,8 +374,7 @@ int bg_attention_peer(const bg_attn_params *p, uint32_t batch, const void *q, ui
   const uint32_t rows = batch * p->S * p->H;
   cudaStream_t st = (cudaStream_t)stream;
   if (pos_hi == pos_lo) {  // this slice attends nothing: push empty rows, then merge the others'
-    int rc = launch_lse_push(nullptr, 0, rows, p->D, x, st);
-    return rc ? rc : launch_lse_merge_peer(x, rows, p->D, gate, out, out_dtype == BG_DT_F16, st);
+    return launch_lse_exchange(nullptr, 0, rows, p->D, x, gate, out, out_dtype == BG_DT_F16, st);
   }
   return run_attention(p, batch, q, q_dtype, kv, nullptr, nullptr, scale, pos_lo, pos_hi, pos_lo, nullptr, gate, out,
                        out_dtype, workspace, workspace_bytes, st, x);

@@ -54,10 +54,10 @@ bool roll_legacy();  // BGATTN_ROLL_LEGACY=1 selects the one-head-per-CTA kernel
 int poll_device_error_attn_tc();
 // Split-KV partial scratch a bg_attention call may need (the part every kernel path shares).
 size_t attention_split_workspace_bytes(const bg_attn_params *p, uint32_t batch);
-int launch_lse_push(const float *partials, uint32_t nsplit, uint32_t rows, uint32_t D, const bg_peer_exchange *x,
-                    cudaStream_t st);
-int launch_lse_merge_peer(const bg_peer_exchange *x, uint32_t rows, uint32_t D, const float *gate, void *out,
-                          int out_f16, cudaStream_t st);
+// Peer-memory split-KV step after the decode kernel: merge this rank's splits of each row, push it
+// to every rank, wait for theirs, merge, gate and write (splitkv_peer.cu).
+int launch_lse_exchange(const float *partials, uint32_t nsplit, uint32_t rows, uint32_t D, const bg_peer_exchange *x,
+                        const float *gate, void *out, int out_f16, cudaStream_t st);
 int poll_device_error_peer();
 PeerArgs peer_args(const bg_peer_exchange *x, uint32_t rows);
 int poll_device_error_attn_roll();

@@ -5,22 +5,23 @@
 // (unnormalised o, m, l) rows of its slice; they have to reach every rank, which then merges them
 // by log-sum-exp and applies the sigmoid gate.  Instead of an NCCL all-gather between two kernels:
 //
-//   push          this rank's split-KV partials are merged (log-sum-exp over its own splits) and
-//                 each finished row is stored straight into every rank's gather buffer over NVLink
-//                 (plain peer stores; no TMA, no multicast); then the row's arrival counter on
-//                 every rank is incremented (system-scope release).
-//   merge         for each row, wait (bounded spin: lane r polls rank r's counter with relaxed
-//                 system-scope loads, then one acquire fence) until every source's counter for
-//                 the row reaches the step number, merge the nranks rows, apply the
-//                 gate; the last CTA to finish advances this rank's step counter.
-// These two kernels are the default step after either decode kernel.  The tensor-core decode
-// kernel can instead do both in its epilogue (the last CTA of each (sequence, kv head) group,
-// found with a per-group ticket, merges, pushes, waits and writes the output; opt-in with
-// BGATTN_PEER_FUSED=1), which makes a step one launch but measured no faster at 2 GPUs.
+//   exchange      one kernel, one CTA per row: this rank's split-KV partials of the row are merged
+//                 (log-sum-exp over its own splits) and the result is stored straight into every
+//                 rank's gather buffer over NVLink (plain peer stores; no TMA, no multicast); the
+//                 row's arrival counter on every rank is incremented (system-scope release); then
+//                 the CTA waits (bounded spin: lane r polls rank r's counter with relaxed
+//                 system-scope loads, then one acquire fence) until every rank's counter for the
+//                 row reaches the step number, merges the nranks rows, applies the gate and writes
+//                 the output; the last CTA to finish advances this rank's step counter.
+// It is the default step after either decode kernel (a separate push and merge kernel pair cost
+// one more kernel boundary, ~2.5 us per step at 2 GPUs).  The tensor-core decode kernel can
+// instead do all of it in its epilogue (the last CTA of each (sequence, kv head) group, found with
+// a per-group ticket; opt-in with BGATTN_PEER_FUSED=1), which measured slower at 2 GPUs.
 //
 // The gather buffers are double-buffered by step parity: rank r can write step e+2 into a peer
-// only after its own merge of step e+1, which needed that peer's step-e+1 rows, which the peer
-// pushes only after its merge of step e -- so a buffer is never overwritten while it is read.
+// only after its own exchange kernel of step e+1 finished, which needed that peer's step-e+1 rows,
+// which the peer pushes only after its exchange of step e finished -- so a buffer is never
+// overwritten while it is read.
 // The step counter lives in device memory, so a captured CUDA graph replays correctly.
 // A wait that runs out records BG_ETIMEOUT (bg_device_status) and the CTA writes zeros.
 #include "attn.h"
@@ -32,8 +33,8 @@ namespace {
 
 #ifdef BG_TRACE
 // Compile-time timing trace (-DBG_TRACE, never in the shipped build), %globaltimer ns of the last
-// step: push CTA r -> [r][0] entry (after its wait), [1] local merge done, [2] counters raised;
-// merge CTA c -> [256 + c][0] entry, [1] rows arrived, [2] done.  Read with bg_ptrace_read.
+// step, exchange CTA r: [r][0] entry (after its wait), [1] local merge done, [2] counters raised,
+// [3] output written, [256 + r][0] every rank's row arrived.  Read with bg_ptrace_read.
 __device__ unsigned long long g_ptrace[512][4];
 __device__ __forceinline__ unsigned long long ptime() {
   unsigned long long t;
@@ -44,19 +45,20 @@ __device__ __forceinline__ unsigned long long ptime() {
 
 // One CTA per row: its 8 warps merge the `nsplit` local partials in one pass (warp w: splits w,
 // w + 8, ..., (m, l, o) loaded in batches of 8 before any arithmetic, a running max per warp), the
-// warp states meet in shared memory rescaled to the common max, and warp 0
-// stores the row into slot (parity, rank) of every rank's gather buffer, then counts it on every
-// rank.  Launched as a programmatic dependent of the decode kernel (griddepcontrol.wait before the
-// first read of the partials).
+// warp states meet in shared memory rescaled to the common max, and warp 0 stores the row into slot
+// (parity, rank) of every rank's gather buffer, counts it on every rank, waits for every rank's
+// row, merges them, gates and writes the output row.  Launched as a programmatic dependent of the
+// decode kernel (griddepcontrol.wait before the first read of the partials).  nsplit == 0: this
+// rank's slice is empty and it pushes an empty row.
 template <int DPL>
-__global__ void __launch_bounds__(256) lse_push_kernel(const float *__restrict__ part, uint32_t nsplit, PeerArgs x) {
+__global__ void __launch_bounds__(256) lse_exchange_kernel(const float *__restrict__ part, uint32_t nsplit, PeerArgs x,
+                                                           const float *__restrict__ gate, void *out, int out_f16) {
   constexpr uint32_t D = DPL * 32;
   __shared__ float red[8][D];
   __shared__ float lsum[8];
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t rows = x.rows, row = blockIdx.x;
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 #ifdef BG_TRACE
   if (threadIdx.x == 0 && row < 256) g_ptrace[row][0] = ptime();
 #endif
@@ -142,47 +144,54 @@ __global__ void __launch_bounds__(256) lse_push_kernel(const float *__restrict__
 #ifdef BG_TRACE
   if (lane == 0 && row < 256) g_ptrace[row][2] = ptime();
 #endif
-}
-
-// One warp per row: wait for every rank's row of this step, merge, gate, write; the last CTA to
-// finish advances the step.
-template <int DPL>
-__global__ void __launch_bounds__(256) lse_merge_peer_kernel(PeerArgs x, const float *__restrict__ gate, void *out,
-                                                             int out_f16) {
-  constexpr uint32_t D = DPL * 32;
-  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const uint32_t rows = x.rows, row = blockIdx.x * 8 + warp;
-  // a programmatic dependent of the push kernel: nothing is read before that grid completed
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // every rank's row of this step (rows written by peers: read past L1)
+  const bool ok = peer_wait_row_warp(x, row, e, &g_device_error, lane);
 #ifdef BG_TRACE
-  if (threadIdx.x == 0 && blockIdx.x < 256) g_ptrace[256 + blockIdx.x][0] = ptime();
+  if (lane == 0 && row < 256) g_ptrace[256 + row][0] = ptime();
 #endif
-  const uint32_t e = *x.step + 1;
-  if (row < rows) {
-    const bool ok = peer_wait_row_warp(x, row, e, &g_device_error, lane);
-#ifdef BG_TRACE
-    if (lane == 0 && warp == 0 && blockIdx.x < 256) g_ptrace[256 + blockIdx.x][1] = ptime();
-#endif
-    float acc[DPL], M = -INFINITY, L = 0.f;
+  // one round trip: every rank's (m, l, o) of the row is loaded before any arithmetic
+  M = -INFINITY;
+  L = 0.f;
 #pragma unroll
-    for (int j = 0; j < DPL; ++j) acc[j] = 0.f;
-    if (ok)  // rows written by peers: read past L1
-      merge_rows<DPL, true>(x.gather[x.rank] + ((uint64_t)(e & 1) * x.nranks * rows + row) * (D + 2),
-                            (uint64_t)rows * (D + 2), x.nranks, lane, acc, M, L);
+  for (int j = 0; j < DPL; ++j) acc[j] = 0.f;
+  if (ok) {
+    const float *src0 = x.gather[x.rank] + ((uint64_t)(e & 1) * x.nranks * rows + row) * (D + 2);
+    float mv[BG_MAX_PEERS], lv[BG_MAX_PEERS], v[BG_MAX_PEERS][DPL];
 #pragma unroll
-    for (int j = 0; j < DPL; ++j) {
-      const uint64_t i = (uint64_t)row * D + lane + 32 * j;
-      float o = L > 0.f ? acc[j] / L : 0.f;
-      if (gate) o = o / (1.0f + expf(-gate[i]));
-      if (out_f16) static_cast<__half *>(out)[i] = __float2half_rn(o);
-      else static_cast<float *>(out)[i] = o;
+    for (int r = 0; r < BG_MAX_PEERS; ++r) {
+      const bool in = r < (int)x.nranks;
+      const float *src = src0 + (uint64_t)(in ? r : 0) * rows * (D + 2);
+      lv[r] = in ? __ldcg(src + D + 1) : 0.f;
+      mv[r] = in ? __ldcg(src + D) : 0.f;
+#pragma unroll
+      for (int j = 0; j < DPL; ++j) v[r][j] = in ? __ldcg(src + lane + 32 * j) : 0.f;
+    }
+#pragma unroll
+    for (int r = 0; r < BG_MAX_PEERS; ++r)
+      if (lv[r] > 0.f) M = fmaxf(M, mv[r]);  // empty rows may hold any bits
+#pragma unroll
+    for (int r = 0; r < BG_MAX_PEERS; ++r) {
+      if (lv[r] > 0.f) {
+        const float f = expf(mv[r] - M);
+        L = fmaf(lv[r], f, L);
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) acc[j] = fmaf(v[r][j], f, acc[j]);
+      }
     }
   }
-  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < DPL; ++j) {
+    const uint64_t i = (uint64_t)row * D + lane + 32 * j;
+    float o = L > 0.f ? acc[j] / L : 0.f;  // a timed-out wait writes zeros
+    if (gate) o = o / (1.0f + expf(-gate[i]));
+    if (out_f16) static_cast<__half *>(out)[i] = __float2half_rn(o);
+    else static_cast<float *>(out)[i] = o;
+  }
 #ifdef BG_TRACE
-  if (threadIdx.x == 0 && blockIdx.x < 256) g_ptrace[256 + blockIdx.x][2] = ptime();
+  if (lane == 0 && row < 256) g_ptrace[row][3] = ptime();
 #endif
-  if (threadIdx.x == 0) {
+  if (lane == 0) {
+    // every CTA has read the step before it counts itself done: the last one advances it
     __threadfence();
     if (atomicAdd(x.done, 1u) == gridDim.x - 1) {
       *x.done = 0;
@@ -223,32 +232,17 @@ PeerArgs peer_args(const bg_peer_exchange *x, uint32_t rows) {
   return a;
 }
 
-int launch_lse_push(const float *partials, uint32_t nsplit, uint32_t rows, uint32_t D, const bg_peer_exchange *x,
-                    cudaStream_t st) {
+int launch_lse_exchange(const float *partials, uint32_t nsplit, uint32_t rows, uint32_t D, const bg_peer_exchange *x,
+                        const float *gate, void *out, int out_f16, cudaStream_t st) {
   const PeerArgs a = peer_args(x, rows);
   if (rows == 0) return BG_OK;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   pdl_config(cfg, attr, dim3(rows), st);
   cudaError_t err;
-  if (D == 64) err = cudaLaunchKernelEx(&cfg, lse_push_kernel<2>, partials, nsplit, a);
-  else if (D == 128) err = cudaLaunchKernelEx(&cfg, lse_push_kernel<4>, partials, nsplit, a);
-  else if (D == 256) err = cudaLaunchKernelEx(&cfg, lse_push_kernel<8>, partials, nsplit, a);
-  else return BG_EUNSUPPORTED;
-  return err == cudaSuccess ? BG_OK : BG_ELAUNCH;
-}
-
-int launch_lse_merge_peer(const bg_peer_exchange *x, uint32_t rows, uint32_t D, const float *gate, void *out,
-                          int out_f16, cudaStream_t st) {
-  const PeerArgs a = peer_args(x, rows);
-  const uint32_t blocks = (rows + 7) / 8;
-  cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
-  pdl_config(cfg, attr, dim3(blocks), st);
-  cudaError_t err;
-  if (D == 64) err = cudaLaunchKernelEx(&cfg, lse_merge_peer_kernel<2>, a, gate, out, out_f16);
-  else if (D == 128) err = cudaLaunchKernelEx(&cfg, lse_merge_peer_kernel<4>, a, gate, out, out_f16);
-  else if (D == 256) err = cudaLaunchKernelEx(&cfg, lse_merge_peer_kernel<8>, a, gate, out, out_f16);
+  if (D == 64) err = cudaLaunchKernelEx(&cfg, lse_exchange_kernel<2>, partials, nsplit, a, gate, out, out_f16);
+  else if (D == 128) err = cudaLaunchKernelEx(&cfg, lse_exchange_kernel<4>, partials, nsplit, a, gate, out, out_f16);
+  else if (D == 256) err = cudaLaunchKernelEx(&cfg, lse_exchange_kernel<8>, partials, nsplit, a, gate, out, out_f16);
   else return BG_EUNSUPPORTED;
   return err == cudaSuccess ? BG_OK : BG_ELAUNCH;
 }
